@@ -1,0 +1,281 @@
+"""Python host binding of libbbh.so (ctypes over the C ABI in include/bbh.h).
+
+Mirrors the reference's host API for the embedding path (tytrdev/bert-by-hand
+src/model/forward.h:11-19 bert_encode / bert_embed, weights.h load_model_weights,
+workspace.h make_workspace) plus the packed variable-length form and the unit
+operators (src/kernels/*.h launch_*). PyTorch is used only to own device memory and
+to name the current CUDA stream; all compute runs in libbbh.so's kernels.
+
+There is no fallback: if libbbh.so is missing or the device is not sm_100, calls raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libbbh.so")
+HIDDEN = 384
+
+BBH_OK = 0
+ERRORS = {-1: "BBH_ERR_ARG", -2: "BBH_ERR_CAPACITY", -3: "BBH_ERR_CUDA", -4: "BBH_ERR_IO",
+          -5: "BBH_ERR_DEVICE", -6: "BBH_ERR_UNSUPPORTED"}
+DEVICE_ERRORS = {0: "ok", 1: "wait timeout", 2: "token or type id out of range",
+                 3: "malformed cu_seqlens", 4: "sequence longer than the position table"}
+
+_lib = None
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_SIGS = {
+    "bbh_last_error": (ctypes.c_char_p, []),
+    "bbh_num_tensors": (_I, [_I]),
+    "bbh_tensor_name": (ctypes.c_char_p, [_I, _I]),
+    "bbh_tensor_numel": (ctypes.c_int64, [_I, _I]),
+    "bbh_weights_load": (_I, [ctypes.c_char_p, _I, _I, ctypes.POINTER(_P)]),
+    "bbh_weights_from_host": (_I, [ctypes.POINTER(_P), _I, _I, ctypes.POINTER(_P)]),
+    "bbh_weights_free": (None, [_P]),
+    "bbh_weights_layers": (_I, [_P]),
+    "bbh_ws_create": (_I, [_P, _I, _I, _I, ctypes.POINTER(_P)]),
+    "bbh_ws_free": (None, [_P]),
+    "bbh_ws_set_graph": (_I, [_P, _I]),
+    "bbh_device_error": (_I, [_P, _I]),
+    "bbh_launches_per_forward": (_I, [_P]),
+    "bbh_embed": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P]),
+    "bbh_encode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P]),
+    "bbh_embed_varlen": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
+    "bbh_encode_varlen": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P]),
+    "bbh_linear": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "bbh_linear_residual_layernorm": (_I, [_P, _P, _P, _P, _P, _P, ctypes.c_float, _P, _I, _I, _P]),
+    "bbh_layernorm": (_I, [_P, _P, _P, _P, _I, _I, ctypes.c_float, _P, _P]),
+    "bbh_attention_varlen": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "bbh_mean_pool_l2": (_I, [_P, _P, _P, _I, _P, _P]),
+}
+
+
+class BBHError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+def lib() -> ctypes.CDLL:
+    """Load libbbh.so (raises if it was not built: run bert-by-hand_b200/build.py)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python bert-by-hand_b200/build.py`")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def _check(rc: int) -> None:
+    if rc != BBH_OK:
+        raise BBHError(rc, lib().bbh_last_error().decode())
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError("expected a contiguous tensor")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _i32(t):
+    if t is None:
+        return None
+    if t.dtype != torch.int32:
+        raise TypeError("token arrays must be int32")
+    return _ptr(t)
+
+
+def _f16(t):
+    if t is None:
+        return None
+    if t.dtype != torch.float16:
+        raise TypeError("expected float16")
+    return _ptr(t)
+
+
+def tensor_names(layers: int = 6) -> list[str]:
+    L = lib()
+    return [L.bbh_tensor_name(layers, i).decode() for i in range(L.bbh_num_tensors(layers))]
+
+
+class ModelWeights:
+    """Device-resident weights (reference: ModelWeights, src/model/weights.h:15-107)."""
+
+    def __init__(self, handle, layers: int, device: int):
+        self.handle = handle
+        self.layers = layers
+        self.device = device
+
+    @classmethod
+    def load(cls, directory: str, layers: int = 6, device: int = 0) -> "ModelWeights":
+        """load_model_weights(): reads <directory>/<HF key>.bin fp16 files."""
+        h = _P()
+        _check(lib().bbh_weights_load(directory.encode(), layers, device, ctypes.byref(h)))
+        return cls(h, layers, device)
+
+    @classmethod
+    def from_numpy(cls, weights: dict, layers: int = 6, device: int = 0) -> "ModelWeights":
+        """From a {HF key: fp16 ndarray} dict (the same tensors the .bin files hold)."""
+        names = tensor_names(layers)
+        keep = [np.ascontiguousarray(weights[n], dtype=np.float16) for n in names]
+        arr = (_P * len(names))(*[a.ctypes.data for a in keep])
+        h = _P()
+        _check(lib().bbh_weights_from_host(arr, layers, device, ctypes.byref(h)))
+        return cls(h, layers, device)
+
+    def free(self):
+        if self.handle:
+            lib().bbh_weights_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Workspace:
+    """Allocate-once activation workspace (reference: Workspace, src/model/workspace.h:10-36)."""
+
+    def __init__(self, weights: ModelWeights, max_tokens: int, max_batch: int, max_len: int, graph: bool = True):
+        self.weights = weights
+        self.max_tokens, self.max_batch, self.max_len = max_tokens, max_batch, max_len
+        h = _P()
+        _check(lib().bbh_ws_create(weights.handle, max_tokens, max_batch, max_len, ctypes.byref(h)))
+        self.handle = h
+        self.set_graph(graph)
+
+    def set_graph(self, enable: bool):
+        _check(lib().bbh_ws_set_graph(self.handle, 1 if enable else 0))
+
+    @property
+    def launches_per_forward(self) -> int:
+        return lib().bbh_launches_per_forward(self.handle)
+
+    def device_error(self, reset: bool = True) -> int:
+        rc = lib().bbh_device_error(self.handle, 1 if reset else 0)
+        if rc < 0:
+            _check(rc)
+        return rc
+
+    # ---- padded (reference layout) ---------------------------------------------------
+    def embed(self, ids, types=None, mask=None, out=None, stream=None):
+        """bert_embed: ids/types/mask int32 [B, S] on device -> fp16 [B, 384]."""
+        B, S = ids.shape
+        out = out if out is not None else torch.empty((B, HIDDEN), dtype=torch.float16, device=ids.device)
+        _check(lib().bbh_embed(self.handle, self.weights.handle, _i32(ids), _i32(types), _i32(mask), _f16(out),
+                               B, S, _stream(stream)))
+        return out
+
+    def encode(self, ids, types=None, mask=None, out=None, stream=None):
+        """bert_encode: -> fp16 [B*S, 384] final hidden states."""
+        B, S = ids.shape
+        out = out if out is not None else torch.empty((B * S, HIDDEN), dtype=torch.float16, device=ids.device)
+        _check(lib().bbh_encode(self.handle, self.weights.handle, _i32(ids), _i32(types), _i32(mask), _f16(out),
+                                B, S, _stream(stream)))
+        return out
+
+    # ---- packed variable length --------------------------------------------------------
+    def embed_varlen(self, ids, types, cu_seqlens, max_len: int, out=None, stream=None):
+        B = cu_seqlens.numel() - 1
+        out = out if out is not None else torch.empty((B, HIDDEN), dtype=torch.float16, device=ids.device)
+        _check(lib().bbh_embed_varlen(self.handle, self.weights.handle, _i32(ids), _i32(types), _i32(cu_seqlens),
+                                      B, ids.numel(), max_len, _f16(out), _stream(stream)))
+        return out
+
+    def encode_varlen(self, ids, types, cu_seqlens, max_len: int, dump_layers: bool = False, stream=None):
+        B = cu_seqlens.numel() - 1
+        T = ids.numel()
+        out = torch.empty((T, HIDDEN), dtype=torch.float16, device=ids.device)
+        dump = (torch.empty((self.weights.layers + 1, T, HIDDEN), dtype=torch.float16, device=ids.device)
+                if dump_layers else None)
+        _check(lib().bbh_encode_varlen(self.handle, self.weights.handle, _i32(ids), _i32(types), _i32(cu_seqlens),
+                                       B, T, max_len, _f16(out), _f16(dump), _stream(stream)))
+        return (out, dump) if dump_layers else out
+
+    def free(self):
+        if self.handle:
+            lib().bbh_ws_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+# ---- unit operators ---------------------------------------------------------------------
+def linear(A, W, bias=None, gelu=False, stream=None):
+    """launch_matmul: A [M,K] @ W[N,K]^T (+bias) (+gelu) on the tcgen05 GEMM."""
+    M, K = A.shape
+    N = W.shape[0]
+    C = torch.empty((M, N), dtype=torch.float16, device=A.device)
+    _check(lib().bbh_linear(_f16(A), _f16(W), _f16(bias), _f16(C), M, N, K, 1 if gelu else 0, _stream(stream)))
+    return C
+
+
+def linear_residual_layernorm(A, W, bias, residual, gamma, beta, eps=1e-12, stream=None):
+    M, K = A.shape
+    C = torch.empty((M, HIDDEN), dtype=torch.float16, device=A.device)
+    _check(lib().bbh_linear_residual_layernorm(_f16(A), _f16(W), _f16(bias), _f16(residual), _f16(gamma),
+                                               _f16(beta), eps, _f16(C), M, K, _stream(stream)))
+    return C
+
+
+def layernorm(x, gamma, beta, eps=1e-12, residual=None, stream=None):
+    M, D = x.shape
+    y = torch.empty_like(x)
+    _check(lib().bbh_layernorm(_f16(x), _f16(gamma), _f16(beta), _f16(y), M, D, eps, _f16(residual),
+                               _stream(stream)))
+    return y
+
+
+def attention_varlen(qkv, cu_seqlens, max_len: int, keymask=None, stream=None):
+    T = qkv.shape[0]
+    ctx = torch.empty((T, HIDDEN), dtype=torch.float16, device=qkv.device)
+    km = None
+    if keymask is not None:
+        if keymask.dtype != torch.uint8:
+            raise TypeError("keymask must be uint8")
+        km = _ptr(keymask)
+    _check(lib().bbh_attention_varlen(_f16(qkv), _f16(ctx), _i32(cu_seqlens), km, cu_seqlens.numel() - 1, max_len,
+                                      _stream(stream)))
+    return ctx
+
+
+def mean_pool_l2(hidden, cu_seqlens, tokmask=None, stream=None):
+    B = cu_seqlens.numel() - 1
+    emb = torch.empty((B, HIDDEN), dtype=torch.float16, device=hidden.device)
+    tm = None
+    if tokmask is not None:
+        if tokmask.dtype != torch.uint8:
+            raise TypeError("tokmask must be uint8")
+        tm = _ptr(tokmask)
+    _check(lib().bbh_mean_pool_l2(_f16(hidden), _i32(cu_seqlens), tm, B, _f16(emb), _stream(stream)))
+    return emb

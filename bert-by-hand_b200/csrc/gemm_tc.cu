@@ -1,0 +1,399 @@
+// Persistent tcgen05 GEMM for the encoder's four dense layers:
+//   C[rows, N] = A[rows, K] . W[N, K]^T + bias   (+ erf-GELU | + residual, LayerNorm)
+// Replaces the reference's wmma GEMM (src/kernels/matmul.cu:94-186) and, for the two
+// N=384 projections, also its residual LayerNorm (src/kernels/layernorm.cu:17-59,
+// called at src/model/encoder.cu:49-50 and :63-64).
+//
+// Design (sm_100a):
+//  * one CTA per SM, persistent over 128 x BN output tiles (row count may be read from
+//    device memory so a captured graph serves every batch shape);
+//  * warp 0 = TMA producer (128B-swizzled K-major tiles into a STAGES-deep ring);
+//  * warp 1 = MMA issuer: one thread issues tcgen05.mma kind::f16 (fp16 in, fp32 TMEM
+//    accumulator), frees ring slots and publishes finished accumulators with
+//    tcgen05.commit;
+//  * warps 2..5 = epilogue: tcgen05.ld 32 columns at a time, bias / GELU / residual +
+//    two-pass LayerNorm in fp32, fp16 stores. Two TMEM accumulators (when 2*BN <= 512)
+//    let the MMA of tile i+1 overlap the epilogue of tile i.
+#include "common.cuh"
+#include "internal.h"
+#include "../../include/bbh.h"
+
+#include <cstdio>
+#include <mutex>
+
+namespace bbh {
+
+template <int BN, int EPI>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;  // 64 fp16 = one 128-byte swizzle row
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+  static constexpr int NACC = (2 * BN <= 512) ? 2 : 1;
+  static constexpr int TMEM_COLS = 512;  // power of two >= NACC*BN for every BN used here
+  static constexpr int MMA_N = BN <= 256 ? BN : BN / 2;
+  static constexpr int N_MMA = BN / MMA_N;
+  static constexpr int TMA_B_ROWS = BN <= 256 ? BN : BN / 2;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+  static_assert(BN % 16 == 0 && MMA_N <= 256, "bad BN");
+  static_assert(NACC * BN <= TMEM_COLS, "TMEM overflow");
+  static_assert(EPI != kEpiResLN || BN == kHidden, "LayerNorm epilogue needs the full 384-wide row");
+};
+
+constexpr int kGemmThreads = 192;
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  using Cfg = GemmCfg<BN, EPI>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int NACC = Cfg::NACC;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accf_bar = empty_bar + STAGES;
+  uint64_t* acce_bar = accf_bar + NACC;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce_bar + NACC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int rows = p.rows_dev ? *p.rows_dev : p.rows;
+  const int m_tiles = (rows + Cfg::BM - 1) / Cfg::BM;
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + Cfg::BK - 1) / Cfg::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < NACC; ++a) {
+      mbar_init(&accf_bar[a], 1);
+      mbar_init(&acce_bar[a], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * Cfg::BM;
+        const int n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err)) break;
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full_bar[stage], kb * Cfg::BK, m0);
+#pragma unroll
+          for (int h = 0; h < BN / Cfg::TMA_B_ROWS; ++h)
+            tma_load_2d(sB + stage * Cfg::B_BYTES + h * Cfg::TMA_B_ROWS * 128, &tmB, &full_bar[stage],
+                        kb * Cfg::BK, n0 + h * Cfg::TMA_B_ROWS);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, Cfg::MMA_N);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 16; ++k) {
+            const uint64_t adesc = sw128_kmajor_desc(a_addr + k * 32);
+#pragma unroll
+            for (int h = 0; h < Cfg::N_MMA; ++h) {
+              const uint64_t bdesc = sw128_kmajor_desc(b_addr + h * Cfg::MMA_N * 128 + k * 32);
+              tc_mma_f16(d_tmem + h * Cfg::MMA_N, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&accf_bar[acc]);
+        if (++acc == NACC) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(&accf_bar[acc], acc_phase, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int m0 = (tile / n_tiles) * Cfg::BM;
+      const int n0 = (tile % n_tiles) * BN;
+      const int row = m0 + quad * 32 + lane;
+      const bool row_ok = row < rows;
+      const uint32_t tacc = tmem_base + lane_off + acc * BN;
+
+      if constexpr (EPI == kEpiResLN) {
+        // pass 1: v = acc + bias + residual, written back to TMEM; row sum
+        const __half* res = p.residual + static_cast<size_t>(row_ok ? row : 0) * p.ldr;
+        float sum = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tacc + c * 32, v);
+          const int col0 = n0 + c * 32;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float b8[8], r8[8];
+            unpack_half8(__ldg(reinterpret_cast<const uint4*>(p.bias + col0) + j), b8);
+            if (row_ok) {
+              unpack_half8(*(reinterpret_cast<const uint4*>(res + col0) + j), r8);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) r8[e] = 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              v[j * 8 + e] += b8[e] + r8[e];
+              sum += v[j * 8 + e];
+            }
+          }
+          tmem_st32(tacc + c * 32, v);
+        }
+        const float mean = sum * (1.0f / BN);
+        // pass 2: centred sum of squares
+        float sq = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tacc + c * 32, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float d = v[j] - mean;
+            sq += d * d;
+          }
+        }
+        const float rstd = rsqrtf(sq * (1.0f / BN) + p.eps);
+        // pass 3: normalise, affine, store
+        __half* out = p.C + static_cast<size_t>(row) * p.ldc;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tacc + c * 32, v);
+          const int col0 = n0 + c * 32;
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float g8[8], b8[8];
+              unpack_half8(__ldg(reinterpret_cast<const uint4*>(p.gamma + col0) + j), g8);
+              unpack_half8(__ldg(reinterpret_cast<const uint4*>(p.beta + col0) + j), b8);
+              uint4 o;
+              uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float y0 = (v[j * 8 + 2 * e] - mean) * rstd * g8[2 * e] + b8[2 * e];
+                const float y1 = (v[j * 8 + 2 * e + 1] - mean) * rstd * g8[2 * e + 1] + b8[2 * e + 1];
+                ow[e] = pack_half2(y0, y1);
+              }
+              *(reinterpret_cast<uint4*>(out + col0) + j) = o;
+            }
+          }
+        }
+      } else {
+        __half* out = p.C + static_cast<size_t>(row) * p.ldc;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tacc + c * 32, v);
+          const int col0 = n0 + c * 32;
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int col = col0 + j * 8;
+              if (col + 8 <= p.N) {
+                float b8[8];
+                if (p.bias) {
+                  unpack_half8(__ldg(reinterpret_cast<const uint4*>(p.bias + col)), b8);
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) b8[e] = 0.f;
+                }
+                uint4 o;
+                uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  float y0 = v[j * 8 + 2 * e] + b8[2 * e];
+                  float y1 = v[j * 8 + 2 * e + 1] + b8[2 * e + 1];
+                  if constexpr (EPI == kEpiGelu) {
+                    y0 = gelu_erf(y0);
+                    y1 = gelu_erf(y1);
+                  }
+                  ow[e] = pack_half2(y0, y1);
+                }
+                *reinterpret_cast<uint4*>(out + col) = o;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acce_bar[acc]);
+      if (++acc == NACC) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && warp == 0 && lane == 0) {
+    // Let in-flight TMA copies land before the CTA's shared memory is released.
+    const unsigned long long t0 = globaltimer();
+    while (globaltimer() - t0 < 1000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ======================================================================== host side
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(ptr);
+  });
+  return fn;
+}
+
+// Row-major [rows, cols] fp16 matrix with row stride ld elements; box = 64 x box_rows,
+// 128-byte swizzle (matches sw128_kmajor_desc).
+static int encode_kmajor(CUtensorMap* map, const __half* base, int rows, int cols, int ld, int box_rows) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return BBH_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16) return BBH_ERR_ARG;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? BBH_OK : BBH_ERR_CUDA;
+}
+
+template <int BN, int EPI>
+static cudaError_t launch_inst(const GemmPlan& plan, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN, EPI>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  gemm_tc_kernel<BN, EPI><<<plan.grid, kGemmThreads, Cfg::SMEM, stream>>>(plan.tmA, plan.tmB, plan.p);
+  return cudaGetLastError();
+}
+
+int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const __half* W, int N, int K, int epi,
+                   int num_sms) {
+  if (!plan || !A || !W || rows_cap <= 0 || N <= 0 || K <= 0 || N % 8 || K % 8 || lda < K) return BBH_ERR_ARG;
+  int bn;
+  if (epi == kEpiResLN) {
+    if (N != kHidden) return BBH_ERR_ARG;
+    bn = 384;
+  } else if (N % 256 == 0) {
+    bn = 256;
+  } else if (N % 192 == 0) {
+    bn = 192;
+  } else {
+    bn = 128;
+  }
+  const int box_b = bn <= 256 ? bn : bn / 2;
+  int rc = encode_kmajor(&plan->tmA, A, rows_cap, K, lda, 128);
+  if (rc) return rc;
+  rc = encode_kmajor(&plan->tmB, W, N, K, K, box_b);
+  if (rc) return rc;
+  plan->bn = bn;
+  plan->epi = epi;
+  plan->rows_cap = rows_cap;
+  const int tiles_cap = ((rows_cap + 127) / 128) * ((N + bn - 1) / bn);
+  plan->grid = tiles_cap < num_sms ? tiles_cap : num_sms;
+  GemmParams& p = plan->p;
+  p = GemmParams{};
+  p.N = N;
+  p.K = K;
+  p.eps = 1e-12f;
+  return BBH_OK;
+}
+
+cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream) {
+  switch (plan.epi * 1000 + plan.bn) {
+    case kEpiBias * 1000 + 128: return launch_inst<128, kEpiBias>(plan, stream);
+    case kEpiBias * 1000 + 192: return launch_inst<192, kEpiBias>(plan, stream);
+    case kEpiBias * 1000 + 256: return launch_inst<256, kEpiBias>(plan, stream);
+    case kEpiGelu * 1000 + 128: return launch_inst<128, kEpiGelu>(plan, stream);
+    case kEpiGelu * 1000 + 192: return launch_inst<192, kEpiGelu>(plan, stream);
+    case kEpiGelu * 1000 + 256: return launch_inst<256, kEpiGelu>(plan, stream);
+    case kEpiResLN * 1000 + 384: return launch_inst<384, kEpiResLN>(plan, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace bbh

@@ -1,0 +1,106 @@
+// Internal launch interfaces shared between the kernel translation units and the C ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace bbh {
+
+// ------------------------------------------------------------------ GEMM (tcgen05)
+enum Epilogue : int {
+  kEpiBias = 0,      // C = A W^T + bias
+  kEpiGelu = 1,      // C = gelu_erf(A W^T + bias)
+  kEpiResLN = 2,     // C = LayerNorm(A W^T + bias + residual) * gamma + beta   (N == 384)
+};
+
+struct GemmParams {
+  __half* C;
+  int ldc;
+  int N;
+  int K;
+  const __half* bias;      // [N] or null
+  const __half* residual;  // [rows, ldr] (kEpiResLN)
+  int ldr;
+  const __half* gamma;     // [N] (kEpiResLN)
+  const __half* beta;      // [N] (kEpiResLN)
+  float eps;
+  const int* rows_dev;     // when non-null the row count is read from device memory
+  int rows;                // otherwise this host value is used
+  int* err;                // device error word
+};
+
+struct GemmPlan {
+  CUtensorMap tmA;
+  CUtensorMap tmB;
+  GemmParams p;
+  int bn;
+  int epi;
+  int grid;
+  int rows_cap;
+};
+
+// Builds the tensor maps and picks the tile shape. A: [rows_cap, K] row-major with row
+// stride lda elements; W: [N, K] row-major (nn.Linear layout). Returns 0 or a BBH_ERR_*.
+int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const __half* W, int N, int K, int epi,
+                   int num_sms);
+cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream);
+
+// ------------------------------------------------------------------ other kernels
+// Forward-call description consumed by the first kernel of a forward. It is passed by
+// value, so a captured graph can be re-pointed at new inputs by updating one node.
+struct EmbedParams {
+  const int32_t* ids;         // [T]
+  const int32_t* types;       // [T] or null (all type 0)
+  const int32_t* cu_seqlens;  // [B+1] device, packed mode; null in padded mode
+  const int32_t* mask;        // [B*S] padded mode (null: all real)
+  int batch;
+  int seq;                    // padded mode row length (0 in packed mode)
+  int total;                  // T
+  int max_len;
+  // model
+  const __half* word;
+  const __half* pos;
+  const __half* type;
+  const __half* gamma;
+  const __half* beta;
+  float eps;
+  // outputs
+  __half* out;                // [T, 384]
+  int32_t* ws_cu;             // [B+1] copy of the segment offsets
+  uint8_t* ws_tokmask;        // [T] 1 = real token (attends and is pooled)
+  int32_t* ws_meta;           // {B, T, max_len, 0}
+  int* err;
+};
+cudaError_t launch_embed_ln(const EmbedParams& p, int grid, cudaStream_t stream);
+
+struct AttnParams {
+  const __half* qkv;       // [T, 1152]: Q | K | V, head h at columns h*32
+  __half* ctx;             // [T, 384]
+  const int32_t* cu;       // [B+1]
+  const uint8_t* tokmask;  // [T], null = every key usable
+  const int32_t* meta;     // {B, T, max_len}, or null to use the host values below
+  int batch;
+  int max_len;
+  float scale_log2;        // log2(e) / sqrt(head_dim)
+};
+cudaError_t launch_attention(const AttnParams& p, int grid, cudaStream_t stream);
+int attention_grid(int num_sms);
+
+struct PoolParams {
+  const __half* hidden;    // [T, 384]
+  const int32_t* cu;       // [B+1]
+  const uint8_t* tokmask;  // [T], null = every token pooled
+  const int32_t* meta;     // {B, ...}, or null to use `batch`
+  int batch;
+  __half* emb;             // [B, 384]
+};
+const void* embed_kernel_fn();
+const void* pool_kernel_fn();
+cudaError_t launch_pool_l2(const PoolParams& p, int grid, cudaStream_t stream);
+
+cudaError_t launch_layernorm(const __half* x, const __half* residual, const __half* gamma, const __half* beta,
+                             __half* y, int rows, float eps, cudaStream_t stream);
+
+}  // namespace bbh

@@ -1,0 +1,132 @@
+/* bbh.h -- C ABI of the B200 MiniLM-BERT sentence-embedding engine (libbbh.so).
+ *
+ * Drop-in for the hot path of tytrdev/bert-by-hand: bert_embed / bert_encode, the
+ * per-tensor fp16 weight files and the allocate-once workspace. Plain pointers and
+ * sizes only: token arrays are int32, fp16 tensors are passed as uint16_t bit patterns,
+ * streams are cudaStream_t passed as void* (NULL = legacy default stream). All data
+ * pointers are DEVICE pointers unless stated otherwise, owned by the caller.
+ *
+ * Every function returns BBH_OK (0) or a negative BBH_ERR_* code; bbh_last_error()
+ * gives the message (per thread). Forward calls are asynchronous on the given stream;
+ * input problems only visible on the device (bad token ids, malformed cu_seqlens) are
+ * recorded in the workspace's device error word, read by bbh_device_error().
+ *
+ * Model: MiniLM/BERT encoder, hidden 384, 12 heads x 32, FFN 1536 (erf-GELU),
+ * vocab 30522, 512 positions, 2 token types, post-LN eps 1e-12; 6 or 12 layers
+ * (reference constants: src/core/model_config.h:7-17, made runtime for the layer count).
+ */
+#ifndef BBH_H_
+#define BBH_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BBH_API __attribute__((visibility("default")))
+#else
+#define BBH_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BBH_OK 0
+#define BBH_ERR_ARG (-1)         /* null pointer, bad shape or alignment */
+#define BBH_ERR_CAPACITY (-2)    /* request exceeds the workspace's capacity */
+#define BBH_ERR_CUDA (-3)        /* a CUDA runtime/driver call failed */
+#define BBH_ERR_IO (-4)          /* weight file missing or short */
+#define BBH_ERR_DEVICE (-5)      /* the device flagged bad input or a timed-out wait */
+#define BBH_ERR_UNSUPPORTED (-6) /* no sm_100 device */
+
+#define BBH_HIDDEN 384
+#define BBH_MAX_POSITIONS 512
+
+typedef struct bbh_weights bbh_weights;
+typedef struct bbh_ws bbh_ws;
+
+/* Last error message of the calling thread ("" if none). */
+BBH_API const char* bbh_last_error(void);
+
+/* ---- weights ------------------------------------------------------------------------
+ * Replaces ModelWeights / load_model_weights() (src/model/weights.h:15-107). Reads the
+ * same files: <dir>/<HF state_dict key>.bin, fp16, nn.Linear (out, in) row-major
+ * (written by scripts/dump_weights.py:75-82). Q/K/V are concatenated along the output
+ * dimension into one [1152, 384] projection as detail::load_qkv does (weights.h:40-54);
+ * everything lives in one device arena. */
+BBH_API int bbh_num_tensors(int layers);
+BBH_API const char* bbh_tensor_name(int layers, int index);
+BBH_API int64_t bbh_tensor_numel(int layers, int index);
+BBH_API int bbh_weights_load(const char* dir, int layers, int device, bbh_weights** out);
+/* tensors[i] = host pointer to tensor i (fp16 bits) in bbh_tensor_name() order. */
+BBH_API int bbh_weights_from_host(const uint16_t* const* tensors, int layers, int device, bbh_weights** out);
+BBH_API void bbh_weights_free(bbh_weights* w);
+BBH_API int bbh_weights_layers(const bbh_weights* w);
+
+/* ---- workspace ----------------------------------------------------------------------
+ * Replaces Workspace / make_workspace(batch) (src/model/workspace.h:10-36): every
+ * activation buffer is allocated once, for max_tokens rows (padded: batch*seq; packed:
+ * total real tokens), max_batch sentences and sentences of at most max_len tokens.
+ * Unlike the reference, requests beyond the capacity are rejected with
+ * BBH_ERR_CAPACITY instead of overflowing. One workspace per concurrent stream. */
+BBH_API int bbh_ws_create(const bbh_weights* w, int max_tokens, int max_batch, int max_len, bbh_ws** out);
+BBH_API void bbh_ws_free(bbh_ws* ws);
+/* 1 (default): bbh_embed* replay one captured CUDA graph per workspace; 0: eager launches. */
+BBH_API int bbh_ws_set_graph(bbh_ws* ws, int enable);
+/* Synchronises the device, returns the workspace's device error code (0 = none) and
+ * optionally clears it. */
+BBH_API int bbh_device_error(bbh_ws* ws, int reset);
+/* Number of kernel launches one forward of this workspace's model issues. */
+BBH_API int bbh_launches_per_forward(const bbh_ws* ws);
+
+/* ---- forward ------------------------------------------------------------------------
+ * bert_embed (src/model/forward.h:17-19, forward.cu:44-53): ids/types/mask are
+ * [batch, seq] int32 row-major (padded layout, position = row % seq); emb is
+ * [batch, 384] fp16, unit L2 norm. types may be NULL (all 0), mask may be NULL (all 1).
+ * seq may be any value in [1, 512] (no multiple-of-16 requirement). */
+BBH_API int bbh_embed(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types, const int32_t* mask,
+              uint16_t* emb, int batch, int seq, void* stream);
+/* bert_encode (src/model/forward.h:11-13, forward.cu:20-42): final hidden states
+ * [batch*seq, 384] fp16 into out. */
+BBH_API int bbh_encode(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types, const int32_t* mask,
+               uint16_t* out, int batch, int seq, void* stream);
+/* Packed variable-length form (no counterpart in the reference, which only pads):
+ * ids/types are [total_tokens] (sentences back to back), cu_seqlens [batch+1] device
+ * int32 offsets with cu_seqlens[0] = 0 and cu_seqlens[batch] = total_tokens; max_len
+ * bounds every sentence length. emb is [batch, 384] fp16. */
+BBH_API int bbh_embed_varlen(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
+                     const int32_t* cu_seqlens, int batch, int total_tokens, int max_len, uint16_t* emb,
+                     void* stream);
+/* Packed encode: out [total_tokens, 384]. layer_dump (may be NULL) receives the hidden
+ * state after the embedding LayerNorm and after each layer: [(layers+1), total_tokens, 384]. */
+BBH_API int bbh_encode_varlen(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
+                      const int32_t* cu_seqlens, int batch, int total_tokens, int max_len, uint16_t* out,
+                      uint16_t* layer_dump, void* stream);
+
+/* ---- unit operators (the reference's launch_* kernel API) ---------------------------- */
+/* launch_matmul (src/kernels/matmul.h): C[M,N] = A[M,K] W[N,K]^T (+ bias) (+ erf-GELU).
+ * N, K multiples of 8; 16-byte aligned pointers. */
+BBH_API int bbh_linear(const uint16_t* A, const uint16_t* W, const uint16_t* bias, uint16_t* C, int M, int N, int K,
+               int gelu, void* stream);
+/* matmul + residual LayerNorm fused (encoder.cu:47-50 / 61-64): C = LN(A W^T + bias +
+ * residual) * gamma + beta, N = 384. */
+BBH_API int bbh_linear_residual_layernorm(const uint16_t* A, const uint16_t* W, const uint16_t* bias,
+                                  const uint16_t* residual, const uint16_t* gamma, const uint16_t* beta, float eps,
+                                  uint16_t* C, int M, int K, void* stream);
+/* launch_layernorm (src/kernels/layernorm.h): y = LN(x [+ residual]); D must be 384. */
+BBH_API int bbh_layernorm(const uint16_t* x, const uint16_t* gamma, const uint16_t* beta, uint16_t* y, int M, int D,
+                  float eps, const uint16_t* residual, void* stream);
+/* launch_attention_scores + launch_softmax + launch_attention_context
+ * (src/kernels/attention.h, softmax.h): qkv [T, 1152] -> ctx [T, 384], sentences given
+ * by cu_seqlens [batch+1] (device); keymask [T] uint8 (device, NULL = all keys valid). */
+BBH_API int bbh_attention_varlen(const uint16_t* qkv, uint16_t* ctx, const int32_t* cu_seqlens, const uint8_t* keymask,
+                         int batch, int max_len, void* stream);
+/* launch_mean_pool + launch_l2_normalize (src/kernels/pooling.h, normalize.h) over
+ * packed segments: hidden [T, 384] -> emb [batch, 384]; tokmask as above. */
+BBH_API int bbh_mean_pool_l2(const uint16_t* hidden, const int32_t* cu_seqlens, const uint8_t* tokmask, int batch,
+                     uint16_t* emb, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BBH_H_ */

@@ -1,0 +1,119 @@
+// bert_by_hand.hpp -- C++ drop-in for tytrdev/bert-by-hand's host API, over libbbh.so.
+//
+// Same names, argument order and failure behaviour as the reference:
+//   ModelWeights load_model_weights()                     src/model/weights.h:88-107
+//   Workspace make_workspace(int batch = 1)               src/model/workspace.h:20-36
+//   void bert_encode(ws, w, ids, types, mask, out, batch, seq)   src/model/forward.h:11-13
+//   void bert_embed(ws, w, ids, types, mask, emb, batch, seq)    src/model/forward.h:17-19
+// Pointers are device pointers; calls are asynchronous on the legacy default stream (or
+// the stream given as the optional last argument). As in the reference
+// (src/core/cuda_check.h:7-17) any failure prints a message and aborts. The engine
+// underneath is the packed/graph-captured sm_100a implementation in libbbh.so.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <utility>
+
+#include "bbh.h"
+
+namespace model {
+constexpr int VOCAB_SIZE = 30522;
+constexpr int HIDDEN = 384;
+constexpr int NUM_LAYERS = 6;
+constexpr int NUM_HEADS = 12;
+constexpr int HEAD_DIM = 32;
+constexpr int FFN_DIM = 1536;
+constexpr int MAX_POSITION = 512;
+constexpr int TYPE_VOCAB_SIZE = 2;
+constexpr float LAYER_NORM_EPS = 1e-12f;
+constexpr int SEQ_LEN = 128;
+constexpr const char* WEIGHTS_DIR = "weights";
+}  // namespace model
+
+namespace bbh_detail {
+inline void check(int rc, const char* what) {
+  if (rc != BBH_OK) {
+    std::fprintf(stderr, "%s failed (%d): %s\n", what, rc, bbh_last_error());
+    std::abort();
+  }
+}
+}  // namespace bbh_detail
+
+// Device-resident weights (one arena). Move-only like the reference's DeviceBuffer members.
+struct ModelWeights {
+  bbh_weights* handle = nullptr;
+  ModelWeights() = default;
+  explicit ModelWeights(bbh_weights* h) : handle(h) {}
+  ModelWeights(const ModelWeights&) = delete;
+  ModelWeights& operator=(const ModelWeights&) = delete;
+  ModelWeights(ModelWeights&& o) noexcept : handle(std::exchange(o.handle, nullptr)) {}
+  ModelWeights& operator=(ModelWeights&& o) noexcept {
+    if (this != &o) {
+      bbh_weights_free(handle);
+      handle = std::exchange(o.handle, nullptr);
+    }
+    return *this;
+  }
+  ~ModelWeights() { bbh_weights_free(handle); }
+};
+
+inline ModelWeights load_model_weights(const char* dir = model::WEIGHTS_DIR, int layers = model::NUM_LAYERS,
+                                       int device = 0) {
+  bbh_weights* w = nullptr;
+  bbh_detail::check(bbh_weights_load(dir, layers, device, &w), "load_model_weights");
+  return ModelWeights(w);
+}
+
+// Scratch sized once for batch x seq tokens. The device buffers are created on the first
+// forward (they are tied to the weights' device and GEMM descriptors).
+struct Workspace {
+  int batch = 1;
+  int seq = model::SEQ_LEN;
+  bbh_ws* handle = nullptr;
+  const bbh_weights* bound = nullptr;
+  Workspace(int b, int s) : batch(b), seq(s) {}
+  Workspace(const Workspace&) = delete;
+  Workspace& operator=(const Workspace&) = delete;
+  Workspace(Workspace&& o) noexcept : batch(o.batch), seq(o.seq), handle(std::exchange(o.handle, nullptr)),
+                                      bound(o.bound) {}
+  ~Workspace() { bbh_ws_free(handle); }
+  bbh_ws* get(const ModelWeights& w) {
+    if (!handle) {
+      bbh_detail::check(bbh_ws_create(w.handle, batch * seq, batch, seq, &handle), "make_workspace");
+      bound = w.handle;
+    }
+    return handle;
+  }
+};
+
+inline Workspace make_workspace(int batch = 1, int seq = model::SEQ_LEN) { return Workspace(batch, seq); }
+
+inline void bert_encode(Workspace& ws, const ModelWeights& w, const int32_t* input_ids,
+                        const int32_t* token_type_ids, const int32_t* mask, __half* out, int batch = 1,
+                        int seq = model::SEQ_LEN, cudaStream_t stream = nullptr) {
+  bbh_detail::check(bbh_encode(ws.get(w), w.handle, input_ids, token_type_ids, mask,
+                               reinterpret_cast<uint16_t*>(out), batch, seq, stream),
+                    "bert_encode");
+}
+
+inline void bert_embed(Workspace& ws, const ModelWeights& w, const int32_t* input_ids,
+                       const int32_t* token_type_ids, const int32_t* mask, __half* embedding, int batch = 1,
+                       int seq = model::SEQ_LEN, cudaStream_t stream = nullptr) {
+  bbh_detail::check(bbh_embed(ws.get(w), w.handle, input_ids, token_type_ids, mask,
+                              reinterpret_cast<uint16_t*>(embedding), batch, seq, stream),
+                    "bert_embed");
+}
+
+// Packed variable-length form: ids/types [total_tokens], cu_seqlens [batch + 1] (device).
+inline void bert_embed_varlen(Workspace& ws, const ModelWeights& w, const int32_t* input_ids,
+                              const int32_t* token_type_ids, const int32_t* cu_seqlens, int batch,
+                              int total_tokens, int max_len, __half* embedding, cudaStream_t stream = nullptr) {
+  bbh_detail::check(bbh_embed_varlen(ws.get(w), w.handle, input_ids, token_type_ids, cu_seqlens, batch,
+                                     total_tokens, max_len, reinterpret_cast<uint16_t*>(embedding), stream),
+                    "bert_embed_varlen");
+}
