@@ -80,8 +80,11 @@ const std::vector<Spec>& cached_specs(int layers) {
 bool valid_layers(int layers) { return layers == 6 || layers == 12; }
 
 int g_num_sms(int device) {
+  static int cache[64] = {};
+  if (device >= 0 && device < 64 && cache[device] > 0) return cache[device];
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) n = 148;
+  if (device >= 0 && device < 64) cache[device] = n;
   return n;
 }
 
@@ -101,10 +104,19 @@ int* unit_err_word(int device) {
 }
 
 int check_sm100(int device) {
-  cudaDeviceProp prop;
-  cudaError_t e = cudaGetDeviceProperties(&prop, device);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
-  if (prop.major != 10) return fail(BBH_ERR_UNSUPPORTED, "libbbh needs an sm_100 (B200-class) GPU");
+  static std::mutex mu;
+  static signed char ok[64] = {};  // 0 unknown, 1 sm_100, -1 other
+  if (device < 0 || device >= 64) return fail(BBH_ERR_ARG, "bad device ordinal");
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (ok[device] == 1) return BBH_OK;
+  }
+  int major = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  std::lock_guard<std::mutex> lk(mu);
+  ok[device] = major == 10 ? 1 : -1;
+  if (major != 10) return fail(BBH_ERR_UNSUPPORTED, "libbbh needs an sm_100 (B200-class) GPU");
   return BBH_OK;
 }
 

@@ -11,8 +11,9 @@
 //  * warp 1 = MMA issuer: one thread issues tcgen05.mma kind::f16 (fp16 in, fp32 TMEM
 //    accumulator), frees ring slots and publishes finished accumulators with
 //    tcgen05.commit;
-//  * warps 2..5 = epilogue: tcgen05.ld 32 columns at a time, bias / GELU / residual +
-//    two-pass LayerNorm in fp32, fp16 stores. Two TMEM accumulators (when 2*BN <= 512)
+//  * warps 2..9 = epilogue, two per TMEM lane quadrant (each half the columns):
+//    tcgen05.ld 64 columns at a time, bias / GELU / residual + two-pass LayerNorm in
+//    fp32 (row statistics combined through shared memory), fp16 stores. Two TMEM accumulators (when 2*BN <= 512)
 //    let the MMA of tile i+1 overlap the epilogue of tile i.
 #include "common.cuh"
 #include "internal.h"
@@ -22,6 +23,8 @@
 #include <mutex>
 
 namespace bbh {
+
+constexpr int kMaxBiasCols = 2048;  // bias staged in shared memory when N <= this
 
 template <int BN, int EPI>
 struct GemmCfg {
@@ -36,13 +39,82 @@ struct GemmCfg {
   static constexpr int MMA_N = BN <= 256 ? BN : BN / 2;
   static constexpr int N_MMA = BN / MMA_N;
   static constexpr int TMA_B_ROWS = BN <= 256 ? BN : BN / 2;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+  static constexpr int AUX_BYTES = 256 /*barriers*/ + 4 * kMaxBiasCols /*bias*/ + 8 * kHidden /*gamma, beta*/ +
+                                   2048 /*row statistics*/;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align slack*/ + AUX_BYTES;
   static_assert(BN % 16 == 0 && MMA_N <= 256, "bad BN");
   static_assert(NACC * BN <= TMEM_COLS, "TMEM overflow");
   static_assert(EPI != kEpiResLN || BN == kHidden, "LayerNorm epilogue needs the full 384-wide row");
 };
 
-constexpr int kGemmThreads = 192;
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant, each owning half the columns
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+
+// Bias (+ GELU) on 32 accumulator columns of one row, fp16 store. `bias` points at fp32
+// values (shared memory) or is null.
+template <int EPI>
+__device__ __forceinline__ void epi_store32(const float* v, int col0, bool row_ok, __half* out_row,
+                                            const float* bias, const __half* gbias, int N) {
+  if (!row_ok) return;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int col = col0 + j * 8;
+    if (col + 8 <= N) {
+      float b8[8];
+      if (bias) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) b8[e] = bias[col + e];
+      } else if (gbias) {
+        unpack_half8(__ldg(reinterpret_cast<const uint4*>(gbias + col)), b8);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) b8[e] = 0.f;
+      }
+      uint4 o;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float y0 = v[j * 8 + 2 * e] + b8[2 * e];
+        float y1 = v[j * 8 + 2 * e + 1] + b8[2 * e + 1];
+        if constexpr (EPI == kEpiGelu) {
+          y0 = gelu_fast(y0);
+          y1 = gelu_fast(y1);
+        }
+        ow[e] = pack_half2(y0, y1);
+      }
+      *reinterpret_cast<uint4*>(out_row + col) = o;
+    }
+  }
+}
+
+// v[0..32) += bias + residual (residual: 4 packed uint4 = 32 fp16).
+__device__ __forceinline__ void ln_add32(float* v, const float* bias, const uint4* res4) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float r8[8];
+    unpack_half8(res4[j], r8);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[j * 8 + e] += bias[j * 8 + e] + r8[e];
+  }
+}
+
+__device__ __forceinline__ void ln_store32(const float* v, int col0, bool row_ok, __half* out_row, float mean,
+                                           float rstd, const float* gamma, const float* beta) {
+  if (!row_ok) return;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = col0 + j * 8 + 2 * e;
+      const float y0 = (v[j * 8 + 2 * e] - mean) * rstd * gamma[c] + beta[c];
+      const float y1 = (v[j * 8 + 2 * e + 1] - mean) * rstd * gamma[c + 1] + beta[c + 1];
+      ow[e] = pack_half2(y0, y1);
+    }
+    *(reinterpret_cast<uint4*>(out_row + col0) + j) = o;
+  }
+}
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -50,6 +122,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   using Cfg = GemmCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int NACC = Cfg::NACC;
+  constexpr int HB = BN / 2;  // columns per epilogue warp
+  static_assert(HB % 32 == 0, "epilogue chunking");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -61,6 +135,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* acce_bar = accf_bar + NACC;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce_bar + NACC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* s_bias = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES + 256);  // [kMaxBiasCols]
+  float* s_gamma = s_bias + kMaxBiasCols;                                            // [384]
+  float* s_beta = s_gamma + kHidden;                                                 // [384]
+  float* red = s_beta + kHidden;  // [2 stats][2 halves][128 rows] (LayerNorm)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -78,7 +156,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < NACC; ++a) {
       mbar_init(&accf_bar[a], 1);
-      mbar_init(&acce_bar[a], 128);
+      mbar_init(&acce_bar[a], 32 * kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -86,6 +164,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+  const bool bias_in_smem = p.bias && p.N <= kMaxBiasCols;
+  if (bias_in_smem)
+    for (int i = threadIdx.x; i < p.N; i += blockDim.x) s_bias[i] = __half2float(p.bias[i]);
+  if constexpr (EPI == kEpiResLN) {
+    for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
+      s_gamma[i] = __half2float(p.gamma[i]);
+      s_beta[i] = __half2float(p.beta[i]);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -159,121 +246,94 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    // ------------------------------------------------------------ epilogue (warps 2..9)
+    const int quad = warp & 3;        // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const int rloc = quad * 32 + lane;  // row within the tile
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m0 = (tile / n_tiles) * Cfg::BM;
+      const int c0 = (tile % n_tiles) * BN + half * HB;  // first output column of this warp
+      const int row = m0 + rloc;
+      const bool row_ok = row < rows;
+      uint4 rcur[4];
+      const __half* res_row = nullptr;
+      if constexpr (EPI == kEpiResLN) {
+        res_row = p.residual + static_cast<size_t>(row_ok ? row : 0) * p.ldr + c0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          rcur[j] = row_ok ? *(reinterpret_cast<const uint4*>(res_row) + j) : make_uint4(0, 0, 0, 0);
+      }
       if (!mbar_wait(&accf_bar[acc], acc_phase, abort_flag, p.err)) break;
       tc_fence_after();
-      const int m0 = (tile / n_tiles) * Cfg::BM;
-      const int n0 = (tile % n_tiles) * BN;
-      const int row = m0 + quad * 32 + lane;
-      const bool row_ok = row < rows;
-      const uint32_t tacc = tmem_base + lane_off + acc * BN;
+      const uint32_t tacc = tmem_base + lane_off + acc * BN + half * HB;
+      __half* out_row = p.C + static_cast<size_t>(row_ok ? row : 0) * p.ldc;
 
       if constexpr (EPI == kEpiResLN) {
-        // pass 1: v = acc + bias + residual, written back to TMEM; row sum
-        const __half* res = p.residual + static_cast<size_t>(row_ok ? row : 0) * p.ldr;
-        float sum = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld32(tacc + c * 32, v);
-          const int col0 = n0 + c * 32;
+        // pass 1: v = acc + bias + residual (residual chunk c+1 is loaded while chunk c is
+        // processed; chunk 0 was fetched before the accumulator wait), written back to
+        // TMEM; shifted sums (shift = this warp's first value)
+        float shift = 0.f, s1 = 0.f, s2 = 0.f;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float b8[8], r8[8];
-            unpack_half8(__ldg(reinterpret_cast<const uint4*>(p.bias + col0) + j), b8);
-            if (row_ok) {
-              unpack_half8(*(reinterpret_cast<const uint4*>(res + col0) + j), r8);
-            } else {
+        for (int c = 0; c < HB; c += 32) {
+          uint4 rnext[4];
+          if (c + 32 < HB) {
 #pragma unroll
-              for (int e = 0; e < 8; ++e) r8[e] = 0.f;
-            }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              v[j * 8 + e] += b8[e] + r8[e];
-              sum += v[j * 8 + e];
-            }
+            for (int j = 0; j < 4; ++j)
+              rnext[j] = row_ok ? *(reinterpret_cast<const uint4*>(res_row + c + 32) + j) : make_uint4(0, 0, 0, 0);
           }
-          tmem_st32(tacc + c * 32, v);
-        }
-        const float mean = sum * (1.0f / BN);
-        // pass 2: centred sum of squares
-        float sq = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
           float v[32];
-          tmem_ld32(tacc + c * 32, v);
+          tmem_ld32(tacc + c, v);
+          ln_add32(v, s_bias + c0 + c, rcur);
+          if (c == 0) shift = v[0];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const float d = v[j] - mean;
-            sq += d * d;
+            const float d = v[j] - shift;
+            s1 += d;
+            s2 += d * d;
+          }
+          tmem_st32(tacc + c, *reinterpret_cast<float(*)[32]>(v));
+          if (c + 32 < HB) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) rcur[j] = rnext[j];
           }
         }
-        const float rstd = rsqrtf(sq * (1.0f / BN) + p.eps);
-        // pass 3: normalise, affine, store
-        __half* out = p.C + static_cast<size_t>(row) * p.ldc;
+        // per-half mean and M2, combined with the partner warp (Chan et al. pairwise update)
+        const float mean_h = shift + s1 * (1.0f / HB);
+        const float m2_h = fmaxf(s2 - s1 * s1 * (1.0f / HB), 0.f);
+        red[half * 128 + rloc] = mean_h;
+        red[256 + half * 128 + rloc] = m2_h;
+        named_barrier(1 + quad, 64);
+        const float ma = red[rloc], mb = red[128 + rloc];
+        const float dm = ma - mb;
+        const float mean = 0.5f * (ma + mb);
+        const float m2 = red[256 + rloc] + red[384 + rloc] + dm * dm * (0.25f * BN);
+        const float rstd = rsqrtf(m2 * (1.0f / BN) + p.eps);
+        named_barrier(1 + quad, 64);  // partner done reading before the next tile overwrites
+        // pass 2: normalise, affine, store
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld32(tacc + c * 32, v);
-          const int col0 = n0 + c * 32;
-          if (row_ok) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float g8[8], b8[8];
-              unpack_half8(__ldg(reinterpret_cast<const uint4*>(p.gamma + col0) + j), g8);
-              unpack_half8(__ldg(reinterpret_cast<const uint4*>(p.beta + col0) + j), b8);
-              uint4 o;
-              uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float y0 = (v[j * 8 + 2 * e] - mean) * rstd * g8[2 * e] + b8[2 * e];
-                const float y1 = (v[j * 8 + 2 * e + 1] - mean) * rstd * g8[2 * e + 1] + b8[2 * e + 1];
-                ow[e] = pack_half2(y0, y1);
-              }
-              *(reinterpret_cast<uint4*>(out + col0) + j) = o;
-            }
-          }
+        for (int c = 0; c < HB; c += 64) {
+          float v[64];
+          tmem_ld64(tacc + c, tacc + c + 32, v);
+          ln_store32(v, c0 + c, row_ok, out_row, mean, rstd, s_gamma, s_beta);
+          ln_store32(v + 32, c0 + c + 32, row_ok, out_row, mean, rstd, s_gamma, s_beta);
         }
       } else {
-        __half* out = p.C + static_cast<size_t>(row) * p.ldc;
+        const float* sb = bias_in_smem ? s_bias : nullptr;
+        int c = 0;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (; c + 64 <= HB; c += 64) {
+          float v[64];
+          tmem_ld64(tacc + c, tacc + c + 32, v);
+          epi_store32<EPI>(v, c0 + c, row_ok, out_row, sb, p.bias, p.N);
+          epi_store32<EPI>(v + 32, c0 + c + 32, row_ok, out_row, sb, p.bias, p.N);
+        }
+        if (c < HB) {
           float v[32];
-          tmem_ld32(tacc + c * 32, v);
-          const int col0 = n0 + c * 32;
-          if (row_ok) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int col = col0 + j * 8;
-              if (col + 8 <= p.N) {
-                float b8[8];
-                if (p.bias) {
-                  unpack_half8(__ldg(reinterpret_cast<const uint4*>(p.bias + col)), b8);
-                } else {
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) b8[e] = 0.f;
-                }
-                uint4 o;
-                uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  float y0 = v[j * 8 + 2 * e] + b8[2 * e];
-                  float y1 = v[j * 8 + 2 * e + 1] + b8[2 * e + 1];
-                  if constexpr (EPI == kEpiGelu) {
-                    y0 = gelu_erf(y0);
-                    y1 = gelu_erf(y1);
-                  }
-                  ow[e] = pack_half2(y0, y1);
-                }
-                *reinterpret_cast<uint4*>(out + col) = o;
-              }
-            }
-          }
+          tmem_ld32(tacc + c, v);
+          epi_store32<EPI>(v, c0 + c, row_ok, out_row, sb, p.bias, p.N);
         }
       }
       tc_fence_before();

@@ -70,7 +70,7 @@ struct EmbedParams {
   __half* out;                // [T, 384]
   int32_t* ws_cu;             // [B+1] copy of the segment offsets
   uint8_t* ws_tokmask;        // [T] 1 = real token (attends and is pooled)
-  int32_t* ws_meta;           // {B, T, max_len, 0}
+  int32_t* ws_meta;           // {B, T, max_len, has_mask}
   int* err;
 };
 cudaError_t launch_embed_ln(const EmbedParams& p, int grid, cudaStream_t stream);
@@ -80,7 +80,7 @@ struct AttnParams {
   __half* ctx;             // [T, 384]
   const int32_t* cu;       // [B+1]
   const uint8_t* tokmask;  // [T], null = every key usable
-  const int32_t* meta;     // {B, T, max_len}, or null to use the host values below
+  const int32_t* meta;     // {B, T, max_len, has_mask}, or null to use the host values below
   int batch;
   int max_len;
   float scale_log2;        // log2(e) / sqrt(head_dim)

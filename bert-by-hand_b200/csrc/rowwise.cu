@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kRowThreads) embed_ln_kernel(EmbedParams p) {
       p.ws_meta[0] = p.batch;
       p.ws_meta[1] = p.total;
       p.ws_meta[2] = p.max_len;
-      p.ws_meta[3] = 0;
+      p.ws_meta[3] = p.mask != nullptr ? 1 : 0;  // a key/pool mask is in effect
     }
   }
 
