@@ -44,6 +44,8 @@ _SIGS = {
     "bbh_ws_set_graph": (_I, [_P, _I]),
     "bbh_device_error": (_I, [_P, _I]),
     "bbh_launches_per_forward": (_I, [_P]),
+    "bbh_ws_set_kernel_timing": (_I, [_P, _I]),
+    "bbh_ws_kernel_times": (_I, [_P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
     "bbh_embed": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P]),
     "bbh_encode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P]),
     "bbh_embed_varlen": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
@@ -172,6 +174,18 @@ class Workspace:
 
     def set_graph(self, enable: bool):
         _check(lib().bbh_ws_set_graph(self.handle, 1 if enable else 0))
+
+    KERNEL_KINDS = ("embed_ln", "qkv_gemm", "attention", "o_gemm_ln", "ffn1_gemm_gelu", "ffn2_gemm_ln", "pool_l2")
+
+    def set_kernel_timing(self, enable: bool):
+        _check(lib().bbh_ws_set_kernel_timing(self.handle, 1 if enable else 0))
+
+    def kernel_times(self) -> dict:
+        """{kind: (total ms, launches)} since the last call (synchronises)."""
+        ms = (ctypes.c_double * 7)()
+        n = (ctypes.c_int64 * 7)()
+        _check(lib().bbh_ws_kernel_times(self.handle, ms, n))
+        return {k: (ms[i], n[i]) for i, k in enumerate(self.KERNEL_KINDS)}
 
     @property
     def launches_per_forward(self) -> int:

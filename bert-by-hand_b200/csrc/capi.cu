@@ -7,6 +7,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstdint>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -296,6 +297,11 @@ struct bbh_ws {
   cudaKernelNodeParams kp_embed{}, kp_pool{};
   bbh::EmbedParams ep{};
   bbh::PoolParams pp{};
+  // per-kernel timing
+  bool timing = false;
+  std::vector<cudaEvent_t> ev;  // pairs
+  std::vector<int> ev_kind;
+  size_t ev_used = 0;
 };
 
 namespace {
@@ -335,6 +341,31 @@ void drop_graph(bbh_ws* ws) {
   ws->n_embed = ws->n_pool = nullptr;
 }
 
+// Event pair around one launch when per-kernel timing is on.
+struct KernelMark {
+  bbh_ws* ws;
+  cudaStream_t s;
+  size_t slot = SIZE_MAX;
+  KernelMark(bbh_ws* w, cudaStream_t st, int kind) : ws(w), s(st) {
+    if (!ws->timing) return;
+    if (ws->ev_used + 2 > ws->ev.size()) {
+      for (int i = 0; i < 64; ++i) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) return;
+        ws->ev.push_back(e);
+      }
+      ws->ev_kind.resize(ws->ev.size() / 2);
+    }
+    slot = ws->ev_used;
+    ws->ev_used += 2;
+    ws->ev_kind[slot / 2] = kind;
+    cudaEventRecord(ws->ev[slot], s);
+  }
+  ~KernelMark() {
+    if (slot != SIZE_MAX) cudaEventRecord(ws->ev[slot + 1], s);
+  }
+};
+
 // Enqueue one forward. pool == false stops after the last layer (encode). dump, when
 // non-null, receives (layers+1) snapshots of the hidden state (eager mode only).
 int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh::PoolParams& pp,
@@ -342,7 +373,10 @@ int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh
   using namespace bbh;
   const int L = ws->w->layers;
   const int row_grid = ws->num_sms * 8;
-  BBH_CUDA(launch_embed_ln(ep, row_grid, s));
+  {
+    KernelMark km(ws, s, 0);
+    BBH_CUDA(launch_embed_ln(ep, row_grid, s));
+  }
   const size_t plane = size_t(total) * kHidden;
   if (dump) BBH_CUDA(cudaMemcpyAsync(dump, ws->X, plane * 2, cudaMemcpyDeviceToDevice, s));
   AttnParams ap{};
@@ -354,15 +388,23 @@ int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh
   ap.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(double(kHeadDim)));
   for (int l = 0; l < L; ++l) {
     const GemmPlan* P = &ws->plans[size_t(l) * 4];
-    BBH_CUDA(launch_gemm(P[0], s));
-    BBH_CUDA(launch_attention(ap, attention_grid(ws->num_sms), s));
-    BBH_CUDA(launch_gemm(P[1], s));
-    BBH_CUDA(launch_gemm(P[2], s));
-    BBH_CUDA(launch_gemm(P[3], s));
+    {
+      KernelMark km(ws, s, 1);
+      BBH_CUDA(launch_gemm(P[0], s));
+    }
+    {
+      KernelMark km(ws, s, 2);
+      BBH_CUDA(launch_attention(ap, attention_grid(ws->num_sms), s));
+    }
+    for (int j = 1; j < 4; ++j) {
+      KernelMark km(ws, s, 2 + j);
+      BBH_CUDA(launch_gemm(P[j], s));
+    }
     if (dump) BBH_CUDA(cudaMemcpyAsync(dump + plane * (l + 1), ws->X, plane * 2, cudaMemcpyDeviceToDevice, s));
   }
   if (pool) {
     int grid = ws->max_batch < ws->num_sms * 8 ? ws->max_batch : ws->num_sms * 8;
+    KernelMark km(ws, s, 6);
     BBH_CUDA(launch_pool_l2(pp, grid, s));
   }
   return BBH_OK;
@@ -405,7 +447,7 @@ int capture_graph(bbh_ws* ws, const bbh::EmbedParams& ep, const bbh::PoolParams&
 }
 
 int run_embed(bbh_ws* ws, const bbh::EmbedParams& ep, const bbh::PoolParams& pp, cudaStream_t s) {
-  if (!ws->use_graph) return enqueue_forward(ws, ep, true, pp, nullptr, ep.total, s);
+  if (!ws->use_graph || ws->timing) return enqueue_forward(ws, ep, true, pp, nullptr, ep.total, s);
   if (!ws->exec) {
     int rc = capture_graph(ws, ep, pp);
     if (rc) {
@@ -542,6 +584,7 @@ void bbh_ws_free(bbh_ws* ws) {
   cudaSetDevice(ws->device);
   drop_graph(ws);
   if (ws->cap_stream) cudaStreamDestroy(ws->cap_stream);
+  for (auto e : ws->ev) cudaEventDestroy(e);
   cudaFree(ws->arena);
   cudaSetDevice(prev);
   delete ws;
@@ -562,6 +605,27 @@ int bbh_device_error(bbh_ws* ws, int reset) {
   BBH_CUDA(cudaMemcpy(&v, ws->err, sizeof(int), cudaMemcpyDeviceToHost));
   if (reset && v) BBH_CUDA(cudaMemset(ws->err, 0, sizeof(int)));
   return v;
+}
+
+int bbh_ws_set_kernel_timing(bbh_ws* ws, int enable) {
+  if (!ws) return fail(BBH_ERR_ARG, "null workspace");
+  ws->timing = enable != 0;
+  return BBH_OK;
+}
+
+int bbh_ws_kernel_times(bbh_ws* ws, double* ms, int64_t* counts) {
+  if (!ws || !ms || !counts) return fail(BBH_ERR_ARG, "bbh_ws_kernel_times: bad arguments");
+  BBH_CUDA(cudaSetDevice(ws->device));
+  for (size_t i = 0; i + 1 < ws->ev_used; i += 2) {
+    BBH_CUDA(cudaEventSynchronize(ws->ev[i + 1]));
+    float t = 0.f;
+    BBH_CUDA(cudaEventElapsedTime(&t, ws->ev[i], ws->ev[i + 1]));
+    const int k = ws->ev_kind[i / 2];
+    ms[k] += t;
+    counts[k] += 1;
+  }
+  ws->ev_used = 0;
+  return BBH_OK;
 }
 
 int bbh_launches_per_forward(const bbh_ws* ws) {

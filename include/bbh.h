@@ -77,6 +77,15 @@ BBH_API int bbh_ws_set_graph(bbh_ws* ws, int enable);
 BBH_API int bbh_device_error(bbh_ws* ws, int reset);
 /* Number of kernel launches one forward of this workspace's model issues. */
 BBH_API int bbh_launches_per_forward(const bbh_ws* ws);
+/* Per-kernel timing (the reference's Timer, src/core/timer.h:6-49, per kernel): while
+ * enabled, forwards run as eager launches with a CUDA event pair around every kernel.
+ * bbh_ws_kernel_times synchronises, adds the elapsed milliseconds and launch counts per
+ * kernel kind into ms[BBH_KERNEL_KINDS] / counts[BBH_KERNEL_KINDS] and resets them.
+ * Kinds: 0 embed+LN, 1 QKV GEMM, 2 attention, 3 O GEMM+LN, 4 FFN1 GEMM+GELU,
+ * 5 FFN2 GEMM+LN, 6 pool+L2. */
+#define BBH_KERNEL_KINDS 7
+BBH_API int bbh_ws_set_kernel_timing(bbh_ws* ws, int enable);
+BBH_API int bbh_ws_kernel_times(bbh_ws* ws, double* ms, int64_t* counts);
 
 /* ---- forward ------------------------------------------------------------------------
  * bert_embed (src/model/forward.h:17-19, forward.cu:44-53): ids/types/mask are
