@@ -55,6 +55,8 @@ _SIGS = {
     "bbh_layernorm": (_I, [_P, _P, _P, _P, _I, _I, ctypes.c_float, _P, _P]),
     "bbh_attention_varlen": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bbh_mean_pool_l2": (_I, [_P, _P, _P, _I, _P, _P]),
+    "bbh_embed_varlen_static": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P]),
+    "bbh_static_device_error": (_I, []),
 }
 
 

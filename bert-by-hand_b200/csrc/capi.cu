@@ -811,3 +811,112 @@ int bbh_mean_pool_l2(const uint16_t* hidden, const int32_t* cu_seqlens, const ui
 }
 
 }  // extern "C"
+
+// ====================================================================== no-allocation path
+// bbh_embed_varlen_static: the packed forward with all scratch in one file-scope device
+// array (no cudaMalloc/cudaFree anywhere on this path). Host code must not pass the
+// array's name to a kernel -- in host code it is only a stand-in for the symbol -- so the
+// device address is looked up once per device with cudaGetSymbolAddress.
+
+namespace {
+
+constexpr size_t static_align(size_t n) { return (n + 255) & ~size_t(255); }
+constexpr size_t kStT = BBH_STATIC_MAX_TOKENS;
+constexpr size_t kStOffX = 0;
+constexpr size_t kStOffY = kStOffX + static_align(kStT * bbh::kHidden * 2);
+constexpr size_t kStOffQkv = kStOffY + static_align(kStT * bbh::kHidden * 2);
+constexpr size_t kStOffCtx = kStOffQkv + static_align(kStT * bbh::kQkvLd * 2);
+constexpr size_t kStOffInter = kStOffCtx + static_align(kStT * bbh::kHidden * 2);
+constexpr size_t kStOffTok = kStOffInter + static_align(kStT * bbh::kFfn * 2);
+constexpr size_t kStOffCu = kStOffTok + static_align(kStT);
+constexpr size_t kStOffMeta = kStOffCu + static_align((BBH_STATIC_MAX_BATCH + 1) * 4);
+constexpr size_t kStOffErr = kStOffMeta + static_align(16);
+constexpr size_t kStBytes = kStOffErr + static_align(4);
+
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_bbh_static_scratch[kStBytes];
+
+namespace {
+
+// Device address of g_bbh_static_scratch on `device` (looked up with that device current).
+int static_scratch(int device, uint8_t** out) {
+  static std::mutex mu;
+  static uint8_t* addr[64] = {};
+  if (device < 0 || device >= 64) return fail(BBH_ERR_ARG, "bad device ordinal");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_bbh_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+    addr[device] = static_cast<uint8_t*>(p);
+  }
+  *out = addr[device];
+  return BBH_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bbh_embed_varlen_static(const bbh_weights* w, const int32_t* ids, const int32_t* types,
+                            const int32_t* cu_seqlens, int batch, int total_tokens, int max_len, uint16_t* emb,
+                            void* stream) {
+  if (!w || !ids || !cu_seqlens || !emb) return fail(BBH_ERR_ARG, "bbh_embed_varlen_static: null pointer");
+  if (batch <= 0 || total_tokens < 0 || max_len <= 0)
+    return fail(BBH_ERR_ARG, "bbh_embed_varlen_static: bad batch / total_tokens / max_len");
+  if (total_tokens > BBH_STATIC_MAX_TOKENS || batch > BBH_STATIC_MAX_BATCH || max_len > BBH_MAX_POSITIONS)
+    return fail(BBH_ERR_CAPACITY, "bbh_embed_varlen_static: request exceeds the static scratch (at most " +
+                                      std::to_string(BBH_STATIC_MAX_TOKENS) + " tokens, " +
+                                      std::to_string(BBH_STATIC_MAX_BATCH) + " sentences, 512 per sentence)");
+  BBH_CUDA(cudaSetDevice(w->device));
+  uint8_t* base = nullptr;
+  int rc = static_scratch(w->device, &base);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  // A workspace view of the static array (host-side bookkeeping only).
+  bbh_ws ws;
+  ws.device = w->device;
+  ws.num_sms = g_num_sms(w->device);
+  ws.max_tokens = BBH_STATIC_MAX_TOKENS;
+  ws.max_batch = BBH_STATIC_MAX_BATCH;
+  ws.max_len = BBH_MAX_POSITIONS;
+  ws.X = reinterpret_cast<__half*>(base + kStOffX);
+  ws.Y = reinterpret_cast<__half*>(base + kStOffY);
+  ws.qkv = reinterpret_cast<__half*>(base + kStOffQkv);
+  ws.ctx = reinterpret_cast<__half*>(base + kStOffCtx);
+  ws.inter = reinterpret_cast<__half*>(base + kStOffInter);
+  ws.tokmask = base + kStOffTok;
+  ws.cu = reinterpret_cast<int32_t*>(base + kStOffCu);
+  ws.meta = reinterpret_cast<int32_t*>(base + kStOffMeta);
+  ws.err = reinterpret_cast<int*>(base + kStOffErr);
+  ws.use_graph = false;
+  rc = build_plans(&ws, w);
+  if (rc) return rc;
+
+  // The error word must start at zero; everything else is written before it is read.
+  BBH_CUDA(cudaMemsetAsync(ws.err, 0, sizeof(int), s));
+  bbh::EmbedParams ep = base_embed_params(&ws, w);
+  ep.ids = ids;
+  ep.types = types;
+  ep.cu_seqlens = cu_seqlens;
+  ep.batch = batch;
+  ep.total = total_tokens;
+  ep.max_len = max_len;
+  return enqueue_forward(&ws, ep, true, base_pool_params(&ws, emb), nullptr, total_tokens, s);
+}
+
+int bbh_static_device_error(void) {
+  int dev = 0;
+  BBH_CUDA(cudaGetDevice(&dev));
+  uint8_t* base = nullptr;
+  int rc = static_scratch(dev, &base);
+  if (rc) return rc;
+  BBH_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  BBH_CUDA(cudaMemcpy(&v, base + kStOffErr, sizeof(int), cudaMemcpyDeviceToHost));
+  return v;
+}
+
+}  // extern "C"

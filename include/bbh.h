@@ -134,6 +134,31 @@ BBH_API int bbh_attention_varlen(const uint16_t* qkv, uint16_t* ctx, const int32
 BBH_API int bbh_mean_pool_l2(const uint16_t* hidden, const int32_t* cu_seqlens, const uint8_t* tokmask, int batch,
                      uint16_t* emb, void* stream);
 
+/* ---- forward without device allocation ----------------------------------------------
+ * No counterpart in the reference. Some callers cannot call cudaMalloc: hosts whose own
+ * pool allocator owns all device memory and forbids allocations behind its back, and
+ * latency-critical paths that cannot take the implicit device synchronisation a
+ * cudaMalloc may cause. This variant of bbh_embed_varlen allocates nothing: its scratch
+ * (activations, sentence table, error word) lives in one fixed array of device memory
+ * inside libbbh.so, about 7.5 MB, which every GPU that loads the library keeps until the
+ * process exits. The caller still passes the weights, inputs and output.
+ * Limits: total_tokens <= BBH_STATIC_MAX_TOKENS, batch <= BBH_STATIC_MAX_BATCH,
+ * max_len <= 512; larger requests return BBH_ERR_CAPACITY with a message saying so.
+ * The first call on each device looks up the array's device address (a
+ * cudaGetSymbolAddress with that device current), so make that first call before any
+ * stream capture. All calls share the one array and it keeps the last call's contents:
+ * calls that overlap on the GPU (for example on two streams of the same device) race and
+ * corrupt each other's results, so serialise them. Device-side input errors go to the
+ * array's own error word, cleared at the start of each call; read it with
+ * bbh_static_device_error(). */
+#define BBH_STATIC_MAX_TOKENS 1024
+#define BBH_STATIC_MAX_BATCH 128
+BBH_API int bbh_embed_varlen_static(const bbh_weights* w, const int32_t* ids, const int32_t* types,
+                                    const int32_t* cu_seqlens, int batch, int total_tokens, int max_len,
+                                    uint16_t* emb, void* stream);
+/* Synchronises the current device and returns the static path's device error code. */
+BBH_API int bbh_static_device_error(void);
+
 #ifdef __cplusplus
 }
 #endif
