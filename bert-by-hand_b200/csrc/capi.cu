@@ -312,10 +312,11 @@ int build_plans(bbh_ws* ws, const bbh_weights* w) {
   for (int l = 0; l < w->layers; ++l) {
     const LayerPtrs& L = w->L[l];
     GemmPlan* P = &ws->plans[size_t(l) * 4];
-    int rc = make_gemm_plan(&P[0], ws->X, kHidden, ws->max_tokens, L.qkv_w, kQkvLd, kHidden, kEpiBias, ws->num_sms);
-    if (!rc) rc = make_gemm_plan(&P[1], ws->ctx, kHidden, ws->max_tokens, L.o_w, kHidden, kHidden, kEpiResLN, ws->num_sms);
-    if (!rc) rc = make_gemm_plan(&P[2], ws->Y, kHidden, ws->max_tokens, L.i_w, kFfn, kHidden, kEpiGelu, ws->num_sms);
-    if (!rc) rc = make_gemm_plan(&P[3], ws->inter, kFfn, ws->max_tokens, L.o2_w, kHidden, kFfn, kEpiResLN, ws->num_sms);
+    const int T = ws->max_tokens;
+    int rc = make_gemm_plan(&P[0], ws->X, kHidden, T, L.qkv_w, kQkvLd, kHidden, ws->qkv, kQkvLd, kEpiBias, ws->num_sms);
+    if (!rc) rc = make_gemm_plan(&P[1], ws->ctx, kHidden, T, L.o_w, kHidden, kHidden, ws->Y, kHidden, kEpiResLN, ws->num_sms);
+    if (!rc) rc = make_gemm_plan(&P[2], ws->Y, kHidden, T, L.i_w, kFfn, kHidden, ws->inter, kFfn, kEpiGelu, ws->num_sms);
+    if (!rc) rc = make_gemm_plan(&P[3], ws->inter, kFfn, T, L.o2_w, kHidden, kFfn, ws->X, kHidden, kEpiResLN, ws->num_sms);
     if (rc) return fail(rc, "tensor map encoding failed");
     P[0].p.C = ws->qkv;  P[0].p.ldc = kQkvLd; P[0].p.bias = L.qkv_b;
     P[1].p.C = ws->Y;    P[1].p.ldc = kHidden; P[1].p.bias = L.o_b;
@@ -729,8 +730,8 @@ static int unit_gemm(const uint16_t* A, const uint16_t* W, const uint16_t* bias,
   int rc = current_device(&dev);
   if (rc) return rc;
   GemmPlan plan;
-  rc = make_gemm_plan(&plan, reinterpret_cast<const __half*>(A), K, M, reinterpret_cast<const __half*>(W), N, K, epi,
-                      g_num_sms(dev));
+  rc = make_gemm_plan(&plan, reinterpret_cast<const __half*>(A), K, M, reinterpret_cast<const __half*>(W), N, K,
+                      reinterpret_cast<__half*>(C), N, epi, g_num_sms(dev));
   if (rc) return fail(rc, "bbh_linear: unsupported shape or alignment (N, K must be multiples of 8)");
   plan.p.C = reinterpret_cast<__half*>(C);
   plan.p.ldc = N;

@@ -33,58 +33,94 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = (160 * 1024) / STAGE_BYTES > 8 ? 8 : (160 * 1024) / STAGE_BYTES;
   static constexpr int NACC = (2 * BN <= 512) ? 2 : 1;
   static constexpr int TMEM_COLS = 512;  // power of two >= NACC*BN for every BN used here
   static constexpr int MMA_N = BN <= 256 ? BN : BN / 2;
   static constexpr int N_MMA = BN / MMA_N;
   static constexpr int TMA_B_ROWS = BN <= 256 ? BN : BN / 2;
   static constexpr int AUX_BYTES = 256 /*barriers*/ + 4 * kMaxBiasCols /*bias*/ + 8 * kHidden /*gamma, beta*/ +
-                                   2048 /*row statistics*/;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align slack*/ + AUX_BYTES;
+                                   2048 /*row statistics*/ + 2048 /*peer statistics*/;
+  static constexpr int STAGING_BYTES = 8 * 2 * 2048;  // 8 epilogue warps x 2 buffers x (32 rows x 64 B)
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align slack*/ + STAGING_BYTES + AUX_BYTES;
   static_assert(BN % 16 == 0 && MMA_N <= 256, "bad BN");
   static_assert(NACC * BN <= TMEM_COLS, "TMEM overflow");
-  static_assert(EPI != kEpiResLN || BN == kHidden, "LayerNorm epilogue needs the full 384-wide row");
+  // The LayerNorm epilogue runs on a 2-CTA cluster: each CTA owns half of the 384-wide row
+  // and the two exchange per-row statistics through distributed shared memory.
+  static constexpr int CLUSTER = EPI == kEpiResLN ? 2 : 1;
+  static_assert(EPI != kEpiResLN || BN * 2 == kHidden, "LayerNorm tiles are 128 x 192 per CTA");
 };
 
 constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant, each owning half the columns
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 
-// Bias (+ GELU) on 32 accumulator columns of one row, fp16 store. `bias` points at fp32
-// values (shared memory) or is null.
+// Output path of the epilogue: each warp owns 32 rows; a 32-column chunk of fp16 is
+// written to a per-warp staging buffer in the 64-byte-swizzle layout (16-byte piece c of
+// row r at piece c ^ ((r >> 1) & 3), so the 32 lanes' row writes hit distinct banks), then
+// lane 0 stores the 32 x 32 box with one TMA store. Two buffers per warp alternate; a
+// buffer is rewritten only after the store issued from it has finished reading it.
+struct ChunkStore {
+  uint8_t* buf;       // this warp's 2 x 2048 B
+  const CUtensorMap* map;
+  int lane;
+  int issued = 0;
+
+  __device__ __forceinline__ void put(const uint32_t (&w)[16], int col0, int row0) {
+    uint8_t* b = buf + (issued & 1) * 2048;
+    if (issued >= 2) {
+      if (lane == 0) bulk_wait_read<1>();
+      __syncwarp();
+    }
+    uint8_t* rowp = b + lane * 64;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<uint4*>(rowp + ((c ^ sw) << 4)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map, b, col0, row0);
+      bulk_commit();
+    }
+    ++issued;
+  }
+  __device__ __forceinline__ void drain() {
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+};
+
+// Bias (+ GELU) on 32 accumulator columns, packed to fp16 and handed to the store path.
+// `bias` points at fp32 values in shared memory, or is null (then `gbias`, global fp16).
 template <int EPI>
-__device__ __forceinline__ void epi_store32(const float* v, int col0, bool row_ok, __half* out_row,
-                                            const float* bias, const __half* gbias, int N) {
-  if (!row_ok) return;
+__device__ __forceinline__ void epi_chunk(const float* v, int col0, int row0, ChunkStore& st, const float* bias,
+                                          const __half* gbias, int N) {
+  uint32_t w[16];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int col = col0 + j * 8;
-    if (col + 8 <= N) {
-      float b8[8];
-      if (bias) {
+    float b8[8];
+    if (bias) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) b8[e] = bias[col + e];
-      } else if (gbias) {
-        unpack_half8(__ldg(reinterpret_cast<const uint4*>(gbias + col)), b8);
-      } else {
+      for (int e = 0; e < 8; ++e) b8[e] = bias[col + e];
+    } else if (gbias && col + 8 <= N) {
+      unpack_half8(__ldg(reinterpret_cast<const uint4*>(gbias + col)), b8);
+    } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) b8[e] = 0.f;
+      for (int e = 0; e < 8; ++e) b8[e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float y0 = v[j * 8 + 2 * e] + b8[2 * e];
+      float y1 = v[j * 8 + 2 * e + 1] + b8[2 * e + 1];
+      if constexpr (EPI == kEpiGelu) {
+        y0 = gelu_fast(y0);
+        y1 = gelu_fast(y1);
       }
-      uint4 o;
-      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float y0 = v[j * 8 + 2 * e] + b8[2 * e];
-        float y1 = v[j * 8 + 2 * e + 1] + b8[2 * e + 1];
-        if constexpr (EPI == kEpiGelu) {
-          y0 = gelu_fast(y0);
-          y1 = gelu_fast(y1);
-        }
-        ow[e] = pack_half2(y0, y1);
-      }
-      *reinterpret_cast<uint4*>(out_row + col) = o;
+      w[j * 4 + e] = pack_half2(y0, y1);
     }
   }
+  st.put(w, col0, row0);
 }
 
 // v[0..32) += bias + residual (residual: 4 packed uint4 = 32 fp16).
@@ -98,27 +134,23 @@ __device__ __forceinline__ void ln_add32(float* v, const float* bias, const uint
   }
 }
 
-__device__ __forceinline__ void ln_store32(const float* v, int col0, bool row_ok, __half* out_row, float mean,
-                                           float rstd, const float* gamma, const float* beta) {
-  if (!row_ok) return;
+__device__ __forceinline__ void ln_chunk(const float* v, int col0, int row0, ChunkStore& st, float mean, float rstd,
+                                         const float* gamma, const float* beta) {
+  uint32_t w[16];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint4 o;
-    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int c = col0 + j * 8 + 2 * e;
-      const float y0 = (v[j * 8 + 2 * e] - mean) * rstd * gamma[c] + beta[c];
-      const float y1 = (v[j * 8 + 2 * e + 1] - mean) * rstd * gamma[c + 1] + beta[c + 1];
-      ow[e] = pack_half2(y0, y1);
-    }
-    *(reinterpret_cast<uint4*>(out_row + col0) + j) = o;
+  for (int e = 0; e < 16; ++e) {
+    const int c = col0 + 2 * e;
+    const float y0 = (v[2 * e] - mean) * rstd * gamma[c] + beta[c];
+    const float y1 = (v[2 * e + 1] - mean) * rstd * gamma[c + 1] + beta[c + 1];
+    w[e] = pack_half2(y0, y1);
   }
+  st.put(w, col0, row0);
 }
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, GemmParams p) {
   using Cfg = GemmCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int NACC = Cfg::NACC;
@@ -129,16 +161,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::STAGING_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* accf_bar = empty_bar + STAGES;
   uint64_t* acce_bar = accf_bar + NACC;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce_bar + NACC);
+  uint64_t* xfull_bar = acce_bar + NACC;  // [2] peer statistics arrived (cluster LayerNorm)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xfull_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* s_bias = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES + 256);  // [kMaxBiasCols]
+  uint8_t* s_stage = smem + STAGES * Cfg::STAGE_BYTES;  // epilogue staging, 1024-aligned
+  float* s_bias = reinterpret_cast<float*>(s_stage + Cfg::STAGING_BYTES + 256);  // [kMaxBiasCols]
   float* s_gamma = s_bias + kMaxBiasCols;                                            // [384]
   float* s_beta = s_gamma + kHidden;                                                 // [384]
   float* red = s_beta + kHidden;  // [2 stats][2 halves][128 rows] (LayerNorm)
+  float2* xstat = reinterpret_cast<float2*>(red + 512);  // [2 slots][128 rows] peer (mean, M2)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -146,8 +181,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int rows = p.rows_dev ? *p.rows_dev : p.rows;
   const int m_tiles = (rows + Cfg::BM - 1) / Cfg::BM;
   const int n_tiles = (p.N + BN - 1) / BN;
-  const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (p.K + Cfg::BK - 1) / Cfg::BK;
+  // Tile schedule. Plain: tiles (m, n) in n-fastest order over all CTAs. Cluster: each
+  // 2-CTA cluster walks m-tiles and CTA rank r owns columns [r*BN, (r+1)*BN).
+  const int crank = Cfg::CLUSTER > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int first_tile = Cfg::CLUSTER > 1 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
+  const int tile_step = Cfg::CLUSTER > 1 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
+  const int num_tiles = Cfg::CLUSTER > 1 ? m_tiles : m_tiles * n_tiles;
+  auto tile_m0 = [&](int t) { return (Cfg::CLUSTER > 1 ? t : t / n_tiles) * Cfg::BM; };
+  auto tile_n0 = [&](int t) { return Cfg::CLUSTER > 1 ? crank * BN : (t % n_tiles) * BN; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -158,10 +200,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&accf_bar[a], 1);
       mbar_init(&acce_bar[a], 32 * kEpiWarps);
     }
+    mbar_init(&xfull_bar[0], 128);
+    mbar_init(&xfull_bar[1], 128);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
   }
   if (warp == 1) tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
   const bool bias_in_smem = p.bias && p.N <= kMaxBiasCols;
@@ -175,6 +220,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (Cfg::CLUSTER > 1) cluster_sync_all();  // peers' barriers are initialised
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
@@ -183,9 +229,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles) * Cfg::BM;
-        const int n0 = (tile % n_tiles) * BN;
+      for (int tile = first_tile; tile < num_tiles && !*abort_flag; tile += tile_step) {
+        const int m0 = tile_m0(tile);
+        const int n0 = tile_n0(tile);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err)) break;
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
@@ -209,7 +255,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      for (int tile = first_tile; tile < num_tiles && !*abort_flag; tile += tile_step) {
         if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1, abort_flag, p.err)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -251,11 +297,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int half = (warp - 2) >> 2;  // which half of the tile's columns
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const int rloc = quad * 32 + lane;  // row within the tile
+    ChunkStore cst{s_stage + (warp - 2) * 4096, &tmC, lane};
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int m0 = (tile / n_tiles) * Cfg::BM;
-      const int c0 = (tile % n_tiles) * BN + half * HB;  // first output column of this warp
+    int iter = 0;  // tiles processed by this CTA (peer-statistics slot and phase)
+    for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++iter) {
+      const int m0 = tile_m0(tile);
+      const int c0 = tile_n0(tile) + half * HB;  // first output column of this warp
       const int row = m0 + rloc;
       const bool row_ok = row < rows;
       uint4 rcur[4];
@@ -269,7 +317,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&accf_bar[acc], acc_phase, abort_flag, p.err)) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + lane_off + acc * BN + half * HB;
-      __half* out_row = p.C + static_cast<size_t>(row_ok ? row : 0) * p.ldc;
+      const int row0 = m0 + quad * 32;  // first row of this warp's 32-row slab
 
       if constexpr (EPI == kEpiResLN) {
         // pass 1: v = acc + bias + residual (residual chunk c+1 is loaded while chunk c is
@@ -308,17 +356,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         named_barrier(1 + quad, 64);
         const float ma = red[rloc], mb = red[128 + rloc];
         const float dm = ma - mb;
-        const float mean = 0.5f * (ma + mb);
-        const float m2 = red[256 + rloc] + red[384 + rloc] + dm * dm * (0.25f * BN);
-        const float rstd = rsqrtf(m2 * (1.0f / BN) + p.eps);
+        const float mean_c = 0.5f * (ma + mb);  // this CTA's 192 columns
+        const float m2_c = red[256 + rloc] + red[384 + rloc] + dm * dm * (0.25f * BN);
         named_barrier(1 + quad, 64);  // partner done reading before the next tile overwrites
+        // exchange with the other CTA of the cluster (the other 192 columns)
+        const int slot = iter & 1;
+        if (half == 0) {
+          const uint32_t peer = static_cast<uint32_t>(crank ^ 1);
+          st_cluster_f32x2(mapa_shared(smem_u32(&xstat[slot * 128 + rloc]), peer), mean_c, m2_c);
+          mbar_arrive_remote(mapa_shared(smem_u32(&xfull_bar[slot]), peer));
+        }
+        if (!mbar_wait_cluster(&xfull_bar[slot], (iter >> 1) & 1, abort_flag, p.err)) break;
+        const float2 ps = xstat[slot * 128 + rloc];
+        const float dp = mean_c - ps.x;
+        const float mean = 0.5f * (mean_c + ps.x);
+        const float m2 = m2_c + ps.y + dp * dp * (0.5f * BN);
+        const float rstd = rsqrtf(m2 * (1.0f / kHidden) + p.eps);
         // pass 2: normalise, affine, store
+        int c = 0;
 #pragma unroll 1
-        for (int c = 0; c < HB; c += 64) {
+        for (; c + 64 <= HB; c += 64) {
           float v[64];
           tmem_ld64(tacc + c, tacc + c + 32, v);
-          ln_store32(v, c0 + c, row_ok, out_row, mean, rstd, s_gamma, s_beta);
-          ln_store32(v + 32, c0 + c + 32, row_ok, out_row, mean, rstd, s_gamma, s_beta);
+          ln_chunk(v, c0 + c, row0, cst, mean, rstd, s_gamma, s_beta);
+          ln_chunk(v + 32, c0 + c + 32, row0, cst, mean, rstd, s_gamma, s_beta);
+        }
+        if (c < HB) {
+          float v[32];
+          tmem_ld32(tacc + c, v);
+          ln_chunk(v, c0 + c, row0, cst, mean, rstd, s_gamma, s_beta);
         }
       } else {
         const float* sb = bias_in_smem ? s_bias : nullptr;
@@ -327,13 +393,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (; c + 64 <= HB; c += 64) {
           float v[64];
           tmem_ld64(tacc + c, tacc + c + 32, v);
-          epi_store32<EPI>(v, c0 + c, row_ok, out_row, sb, p.bias, p.N);
-          epi_store32<EPI>(v + 32, c0 + c + 32, row_ok, out_row, sb, p.bias, p.N);
+          epi_chunk<EPI>(v, c0 + c, row0, cst, sb, p.bias, p.N);
+          epi_chunk<EPI>(v + 32, c0 + c + 32, row0, cst, sb, p.bias, p.N);
         }
         if (c < HB) {
           float v[32];
           tmem_ld32(tacc + c, v);
-          epi_store32<EPI>(v, c0 + c, row_ok, out_row, sb, p.bias, p.N);
+          epi_chunk<EPI>(v, c0 + c, row0, cst, sb, p.bias, p.N);
         }
       }
       tc_fence_before();
@@ -343,6 +409,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         acc_phase ^= 1;
       }
     }
+    cst.drain();
   }
 
   tc_fence_before();
@@ -354,6 +421,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
   __syncthreads();
+  if constexpr (Cfg::CLUSTER > 1) cluster_sync_all();  // no peer still writes into this CTA
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -380,18 +448,20 @@ static PFN_encodeTiled get_encode_fn() {
   return fn;
 }
 
-// Row-major [rows, cols] fp16 matrix with row stride ld elements; box = 64 x box_rows,
-// 128-byte swizzle (matches sw128_kmajor_desc).
-static int encode_kmajor(CUtensorMap* map, const __half* base, int rows, int cols, int ld, int box_rows) {
+// Row-major [rows, cols] fp16 matrix with row stride ld elements; box = box_cols x box_rows
+// with the given swizzle (operands: 64 x rows, 128-byte swizzle, matching
+// sw128_kmajor_desc; outputs: 32 x 32, 64-byte swizzle, matching ChunkStore).
+static int encode_2d(CUtensorMap* map, const __half* base, int rows, int cols, int ld, int box_cols, int box_rows,
+                     CUtensorMapSwizzle swz) {
   PFN_encodeTiled enc = get_encode_fn();
   if (!enc) return BBH_ERR_CUDA;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16) return BBH_ERR_ARG;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? BBH_OK : BBH_ERR_CUDA;
 }
@@ -400,24 +470,65 @@ template <int BN, int EPI>
 static cudaError_t launch_inst(const GemmPlan& plan, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, EPI>;
   static bool attr_set[64] = {};
+  static int max_clusters[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
+  auto kern = gemm_tc_kernel<BN, EPI>;
   if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     if (e != cudaSuccess) return e;
+    if constexpr (Cfg::CLUSTER > 1) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+      (void)e;
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = Cfg::CLUSTER;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * 74);
+      cfg.blockDim = dim3(kGemmThreads);
+      cfg.dynamicSmemBytes = Cfg::SMEM;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess || n <= 0) n = 64;
+      max_clusters[dev] = n;
+    }
     attr_set[dev] = true;
   }
-  gemm_tc_kernel<BN, EPI><<<plan.grid, kGemmThreads, Cfg::SMEM, stream>>>(plan.tmA, plan.tmB, plan.p);
-  return cudaGetLastError();
+  if constexpr (Cfg::CLUSTER > 1) {
+    const int m_tiles_cap = (plan.rows_cap + Cfg::BM - 1) / Cfg::BM;
+    int nclusters = dev < 64 ? max_clusters[dev] : 64;
+    if (nclusters > m_tiles_cap) nclusters = m_tiles_cap;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = Cfg::CLUSTER;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(Cfg::CLUSTER * nclusters);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, plan.tmA, plan.tmB, plan.tmC, plan.p);
+  } else {
+    kern<<<plan.grid, kGemmThreads, Cfg::SMEM, stream>>>(plan.tmA, plan.tmB, plan.tmC, plan.p);
+    return cudaGetLastError();
+  }
 }
 
-int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const __half* W, int N, int K, int epi,
-                   int num_sms) {
-  if (!plan || !A || !W || rows_cap <= 0 || N <= 0 || K <= 0 || N % 8 || K % 8 || lda < K) return BBH_ERR_ARG;
+int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const __half* W, int N, int K,
+                   __half* C, int ldc, int epi, int num_sms) {
+  if (!plan || !A || !W || !C || rows_cap <= 0 || N <= 0 || K <= 0 || N % 8 || K % 8 || lda < K || ldc < N)
+    return BBH_ERR_ARG;
   int bn;
   if (epi == kEpiResLN) {
     if (N != kHidden) return BBH_ERR_ARG;
-    bn = 384;
+    bn = 192;  // per CTA of a 2-CTA cluster
   } else if (N % 256 == 0) {
     bn = 256;
   } else if (N % 192 == 0) {
@@ -426,9 +537,11 @@ int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const
     bn = 128;
   }
   const int box_b = bn <= 256 ? bn : bn / 2;
-  int rc = encode_kmajor(&plan->tmA, A, rows_cap, K, lda, 128);
+  int rc = encode_2d(&plan->tmA, A, rows_cap, K, lda, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_kmajor(&plan->tmB, W, N, K, K, box_b);
+  rc = encode_2d(&plan->tmB, W, N, K, K, 64, box_b, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&plan->tmC, C, rows_cap, N, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
   plan->bn = bn;
   plan->epi = epi;
@@ -439,6 +552,8 @@ int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const
   p = GemmParams{};
   p.N = N;
   p.K = K;
+  p.C = C;
+  p.ldc = ldc;
   p.eps = 1e-12f;
   return BBH_OK;
 }
@@ -451,7 +566,7 @@ cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream) {
     case kEpiGelu * 1000 + 128: return launch_inst<128, kEpiGelu>(plan, stream);
     case kEpiGelu * 1000 + 192: return launch_inst<192, kEpiGelu>(plan, stream);
     case kEpiGelu * 1000 + 256: return launch_inst<256, kEpiGelu>(plan, stream);
-    case kEpiResLN * 1000 + 384: return launch_inst<384, kEpiResLN>(plan, stream);
+    case kEpiResLN * 1000 + 192: return launch_inst<192, kEpiResLN>(plan, stream);
     default: return cudaErrorInvalidValue;
   }
 }

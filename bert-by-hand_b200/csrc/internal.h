@@ -34,6 +34,7 @@ struct GemmParams {
 struct GemmPlan {
   CUtensorMap tmA;
   CUtensorMap tmB;
+  CUtensorMap tmC;
   GemmParams p;
   int bn;
   int epi;
@@ -42,9 +43,10 @@ struct GemmPlan {
 };
 
 // Builds the tensor maps and picks the tile shape. A: [rows_cap, K] row-major with row
-// stride lda elements; W: [N, K] row-major (nn.Linear layout). Returns 0 or a BBH_ERR_*.
-int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const __half* W, int N, int K, int epi,
-                   int num_sms);
+// stride lda elements; W: [N, K] row-major (nn.Linear layout); C: [rows_cap, N] with row
+// stride ldc (written by TMA stores, clipped at rows_cap and N). Returns 0 or a BBH_ERR_*.
+int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const __half* W, int N, int K,
+                   __half* C, int ldc, int epi, int num_sms);
 cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream);
 
 // ------------------------------------------------------------------ other kernels
