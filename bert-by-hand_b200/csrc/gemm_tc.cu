@@ -11,7 +11,7 @@
 //  * warp 1 = MMA issuer: one thread issues tcgen05.mma kind::f16 (fp16 in, fp32 TMEM
 //    accumulator), frees ring slots and publishes finished accumulators with
 //    tcgen05.commit;
-//  * warps 2..9 = epilogue, two per TMEM lane quadrant (each half the columns):
+//  * warps 2.. = epilogue, 2 or 3 per TMEM lane quadrant (each a part of the columns):
 //    tcgen05.ld 64 columns at a time, bias / GELU / residual + two-pass LayerNorm in
 //    fp32 (row statistics combined through shared memory), fp16 stores. Two TMEM accumulators (when 2*BN <= 512)
 //    let the MMA of tile i+1 overlap the epilogue of tile i.
@@ -41,7 +41,11 @@ struct GemmCfg {
   static constexpr int TMA_B_ROWS = BN <= 256 ? BN : BN / 2;
   static constexpr int AUX_BYTES = 256 /*barriers*/ + 4 * kMaxBiasCols /*bias*/ + 8 * kHidden /*gamma, beta*/ +
                                    2048 /*row statistics*/ + 2048 /*peer statistics*/;
-  static constexpr int STAGING_BYTES = 8 * 2 * 2048;  // 8 epilogue warps x 2 buffers x (32 rows x 64 B)
+  // epilogue warps: 4 TMEM lane quadrants x PARTS column parts
+  static constexpr int PARTS = (EPI != kEpiResLN && BN == 192) ? 3 : 2;
+  static constexpr int EPI_WARPS = 4 * PARTS;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int STAGING_BYTES = EPI_WARPS * 2 * 2048;  // per warp: 2 buffers x (32 rows x 64 B)
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align slack*/ + STAGING_BYTES + AUX_BYTES;
   static_assert(BN % 16 == 0 && MMA_N <= 256, "bad BN");
   static_assert(NACC * BN <= TMEM_COLS, "TMEM overflow");
@@ -51,8 +55,6 @@ struct GemmCfg {
   static_assert(EPI != kEpiResLN || BN * 2 == kHidden, "LayerNorm tiles are 128 x 192 per CTA");
 };
 
-constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant, each owning half the columns
-constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 
 // Output path of the epilogue: each warp owns 32 rows; a 32-column chunk of fp16 is
 // written to a per-warp staging buffer in the 64-byte-swizzle layout (16-byte piece c of
@@ -148,13 +150,13 @@ __device__ __forceinline__ void ln_chunk(const float* v, int col0, int row0, Chu
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, GemmParams p) {
   using Cfg = GemmCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int NACC = Cfg::NACC;
-  constexpr int HB = BN / 2;  // columns per epilogue warp
+  constexpr int HB = BN / Cfg::PARTS;  // columns per epilogue warp
   static_assert(HB % 32 == 0, "epilogue chunking");
 
   extern __shared__ uint8_t smem_raw[];
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < NACC; ++a) {
       mbar_init(&accf_bar[a], 1);
-      mbar_init(&acce_bar[a], 32 * kEpiWarps);
+      mbar_init(&acce_bar[a], 32 * Cfg::EPI_WARPS);
     }
     mbar_init(&xfull_bar[0], 128);
     mbar_init(&xfull_bar[1], 128);
@@ -294,7 +296,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..9)
     const int quad = warp & 3;        // TMEM lane quadrant this warp may access
-    const int half = (warp - 2) >> 2;  // which half of the tile's columns
+    const int half = (warp - 2) >> 2;  // which column part of the tile (0 .. PARTS-1)
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const int rloc = quad * 32 + lane;  // row within the tile
     ChunkStore cst{s_stage + (warp - 2) * 4096, &tmC, lane};
@@ -487,7 +489,7 @@ static cudaError_t launch_inst(const GemmPlan& plan, cudaStream_t stream) {
       attr[0].val.clusterDim.y = 1;
       attr[0].val.clusterDim.z = 1;
       cfg.gridDim = dim3(2 * 74);
-      cfg.blockDim = dim3(kGemmThreads);
+      cfg.blockDim = dim3(Cfg::THREADS);
       cfg.dynamicSmemBytes = Cfg::SMEM;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
@@ -509,14 +511,14 @@ static cudaError_t launch_inst(const GemmPlan& plan, cudaStream_t stream) {
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(Cfg::CLUSTER * nclusters);
-    cfg.blockDim = dim3(kGemmThreads);
+    cfg.blockDim = dim3(Cfg::THREADS);
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, plan.tmA, plan.tmB, plan.tmC, plan.p);
   } else {
-    kern<<<plan.grid, kGemmThreads, Cfg::SMEM, stream>>>(plan.tmA, plan.tmB, plan.tmC, plan.p);
+    kern<<<plan.grid, Cfg::THREADS, Cfg::SMEM, stream>>>(plan.tmA, plan.tmB, plan.tmC, plan.p);
     return cudaGetLastError();
   }
 }
@@ -529,10 +531,10 @@ int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const
   if (epi == kEpiResLN) {
     if (N != kHidden) return BBH_ERR_ARG;
     bn = 192;  // per CTA of a 2-CTA cluster
-  } else if (N % 256 == 0) {
-    bn = 256;
   } else if (N % 192 == 0) {
     bn = 192;
+  } else if (N % 256 == 0) {
+    bn = 256;
   } else {
     bn = 128;
   }
