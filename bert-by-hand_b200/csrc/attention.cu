@@ -92,7 +92,7 @@ struct Decomp {
   __device__ __forceinline__ bool streamed() const { return qshift > 0; }
 };
 
-__device__ __forceinline__ Unit find_unit(const int* cu, const Decomp& d, int item, int step) {
+__device__ __forceinline__ Unit find_unit(const int* cu, const Decomp& d, int item, int step, int min_len) {
   Unit u;
   for (; item < d.items; item += step) {
     const int qc = d.qc(item);
@@ -100,6 +100,7 @@ __device__ __forceinline__ Unit find_unit(const int* cu, const Decomp& d, int it
     const int b = d.b(item);
     const int start = cu[b];
     const int len = cu[b + 1] - start;
+    if (len < min_len) continue;
     bool active;
     if (d.streamed()) {
       active = qc * kQRows < len && (len > kKeyBlock || qc == 0) && (heads_per_cta(len) == 1 || h % heads_per_cta(len) == 0);
@@ -118,14 +119,14 @@ __device__ __forceinline__ Unit find_unit(const int* cu, const Decomp& d, int it
   return u;
 }
 
-__device__ __forceinline__ Unit next_unit(const int* cu, const Decomp& d, const Unit& u, int step) {
+__device__ __forceinline__ Unit next_unit(const int* cu, const Decomp& d, const Unit& u, int step, int min_len) {
   if (u.item < 0) return u;
   if (u.len > kKeyBlock && (u.kb + 1) * kKeyBlock < u.len) {
     Unit n = u;
     n.kb = u.kb + 1;
     return n;
   }
-  return find_unit(cu, d, u.item + step, step);
+  return find_unit(cu, d, u.item + step, step, min_len);
 }
 
 // Number of query rows an item covers (from q0).
@@ -330,12 +331,12 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_varlen_kernel(AttnP
     cu = s_cu;
   }
 
-  Unit cur = find_unit(cu, d, blockIdx.x, gridDim.x);
+  Unit cur = find_unit(cu, d, blockIdx.x, gridDim.x, p.min_len);
   if (cur.item < 0) return;
   load_unit(p, tokmask, d, cur, bufs[0], tid);
   cp_async_commit();
   int bi = 0;
-  Unit nxt = next_unit(cu, d, cur, gridDim.x);
+  Unit nxt = next_unit(cu, d, cur, gridDim.x, p.min_len);
   SoftmaxState st;
 
   while (cur.item >= 0) {
@@ -372,7 +373,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_varlen_kernel(AttnP
         state_store(st, p, cur.start, cur.len, qb * 16, h0 + slot, lane);
       }
     }
-    const Unit nxt2 = next_unit(cu, d, nxt, gridDim.x);
+    const Unit nxt2 = next_unit(cu, d, nxt, gridDim.x, p.min_len);
     __syncthreads();  // buffer bi is refilled on the next iteration
     cur = nxt;
     nxt = nxt2;

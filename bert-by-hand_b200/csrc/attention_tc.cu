@@ -1,0 +1,358 @@
+// Tensor-core (tcgen05 / TMEM) attention for sentences of at most 128 tokens.
+// Replaces the reference's scores -> masked softmax -> context kernels
+// (src/kernels/attention.cu:17-121, src/kernels/softmax.cu:26-73) for packed varlen input.
+//
+// A CTA of 128 threads processes one 128-row tile at a time. The tile packs G "slots" of
+// Lp rows (Lp = 16, 32, 64 or 128: the smallest power of two >= L, G = 128 / Lp), one per
+// head of the same sentence, so short sentences still fill the MMA rows:
+//   1. Q, K, V slices of the fused QKV buffer go to shared memory with cp.async (64-byte
+//      swizzled rows of 32 fp16; rows past the sentence are zero-filled), double buffered
+//      across tiles.
+//   2. One thread issues S = Q K^T (tcgen05.mma, M = N = 128, K = 32) into TMEM.
+//   3. Thread t owns query row t (TMEM lane t): it reads the columns of its own slot's keys
+//      (a key of another head, or past the sentence end, is dropped), takes the row max in
+//      a first pass over TMEM, then exponentiates in the exp2 domain, sums, and writes its
+//      row of P (fp16) to shared memory in the 128-byte swizzled K-major layout -- no warp
+//      shuffles, no S buffer in global memory. Warps whose 32 rows hold no query skip.
+//   4. One thread issues O = P V (tcgen05.mma, M = 128, N = 32, K = the keys in use, V as
+//      an MN-major operand) into the TMEM columns S used; thread t normalises its row by
+//      its softmax sum and stores the 32 head dimensions to the merged context [T, 384].
+// A key is also dropped where the token mask is 0 (padded calls), as softmax.cu:43-59 does;
+// a row with no usable key gives zeros.
+#include "common.cuh"
+#include "internal.h"
+
+namespace bbh {
+
+constexpr int kTcThreads = 128;
+constexpr int kTcRows = 128;
+constexpr int kTcCuCache = 1152;  // cu_seqlens entries cached in shared memory
+
+struct TcBuf {  // one tile's operands, each 128 rows x 64 B, 64-byte swizzle
+  uint8_t q[kTcRows * 64];
+  uint8_t k[kTcRows * 64];
+  uint8_t v[kTcRows * 64];
+};
+static_assert(sizeof(TcBuf) % 1024 == 0, "swizzled operands must stay 1024-byte aligned");
+
+struct TcSmem {
+  TcBuf buf[2];
+  uint8_t p[2][kTcRows * 128];  // P, keys 0-63 and 64-127, 128-byte swizzle, K-major
+  uint8_t keyok[2][kTcRows];    // 1 = usable key row (padded calls with a token mask)
+  uint64_t bar_s, bar_o;
+  uint32_t tmem;
+  int abort_flag;
+  int cu[1];  // cached cu_seqlens follow (variable length)
+};
+
+// K-major operand with 64-byte rows (32 fp16) and 64-byte swizzle: SBO = 8 rows x 64 B.
+__device__ __forceinline__ uint64_t sw64_kmajor_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr & 0x3FFFF) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;         // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(512 >> 4) << 32;  // SBO
+  d |= static_cast<uint64_t>(1) << 46;         // sm_100 descriptor version
+  d |= static_cast<uint64_t>(4) << 61;         // SWIZZLE_64B
+  return d;
+}
+
+// MN-major operand (V: rows = keys = K dimension, 32 fp16 of N per 64-byte row), 64-byte
+// swizzle: 8 K-rows per 512-byte atom (SBO); one 32-element N group, so LBO is not used.
+__device__ __forceinline__ uint64_t sw64_mnmajor_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr & 0x3FFFF) >> 4);
+  d |= static_cast<uint64_t>(4096 >> 4) << 16;  // LBO: next 32-wide N group (never used, N = 32)
+  d |= static_cast<uint64_t>(512 >> 4) << 32;   // SBO: next 8 K-rows
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(4) << 61;
+  return d;
+}
+
+__device__ __forceinline__ void cp_async16_tc(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_tc() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_tc() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// log2 of the slot height for a sentence of `len` tokens
+__device__ __forceinline__ int slot_log2(int len) { return len <= 16 ? 4 : len <= 32 ? 5 : len <= 64 ? 6 : 7; }
+
+// Items are enumerated head-major, item = h * batch + b: with a grid-stride walk every CTA
+// then meets a mix of sentences and heads. (Sentence-major order aliases with the stride:
+// the packed-head items, h % G == 0, would all land on a quarter of the CTAs.)
+struct TcItem {
+  int item;  // h0 * batch + b, or -1
+  int h0, start, len;
+};
+
+__device__ __forceinline__ TcItem tc_find(const int* cu, int batch, int item, int step, int items) {
+  TcItem u;
+  for (; item < items; item += step) {
+    const int b = item % batch;
+    const int h = item / batch;
+    const int start = cu[b];
+    const int len = cu[b + 1] - start;
+    if (len <= 0 || len > kTcRows) continue;
+    const int G = kTcRows >> slot_log2(len);
+    if (h % G) continue;
+    u.item = item;
+    u.h0 = h;
+    u.start = start;
+    u.len = len;
+    return u;
+  }
+  u.item = -1;
+  return u;
+}
+
+__device__ __forceinline__ void tc_load(const AttnParams& p, const uint8_t* tokmask, const TcItem& u, TcBuf& B,
+                                        uint8_t* keyok, int tid) {
+  const int lg = slot_log2(u.len);
+  const int G = kTcRows >> lg;
+  const int h0 = u.h0;
+  const int nh = (kHeads - h0) < G ? (kHeads - h0) : G;
+  const __half* base = p.qkv + static_cast<size_t>(u.start) * kQkvLd + h0 * kHeadDim;
+  const uint32_t sq = smem_u32(B.q), sk = smem_u32(B.k), sv = smem_u32(B.v);
+  // 128 rows x 4 pieces per operand; thread tid handles piece (tid & 3) of rows tid/4 + 32 i
+  const int c = tid & 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = (tid >> 2) + 32 * i;
+    const int s = r >> lg, q = r & ((1 << lg) - 1);
+    const bool ok = s < nh && q < u.len;
+    const __half* src = base + static_cast<size_t>(ok ? q : 0) * kQkvLd + s * kHeadDim + c * 8;
+    const uint32_t off = r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
+    cp_async16_tc(sq + off, src, ok ? 16 : 0);
+    cp_async16_tc(sk + off, src + kHidden, ok ? 16 : 0);
+    cp_async16_tc(sv + off, src + 2 * kHidden, ok ? 16 : 0);
+  }
+  if (tokmask) {
+    const int r = tid;
+    const int s = r >> lg, q = r & ((1 << lg) - 1);
+    keyok[r] = (s < nh && q < u.len) ? tokmask[u.start + q] : 0;
+  }
+}
+
+__device__ __forceinline__ void store_p_piece(TcSmem& sm, int tid, int pc, uint4 w) {
+  *reinterpret_cast<uint4*>(sm.p[pc >> 3] + tid * 128 + (((pc & 7) ^ (tid & 7)) << 4)) = w;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 2) attention_tc_kernel(AttnParams p) {
+  extern __shared__ uint8_t tc_raw[];
+  TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+
+  const int batch = p.meta ? p.meta[0] : p.batch;
+  const uint8_t* tokmask = (p.meta && p.meta[3] == 0) ? nullptr : p.tokmask;
+  const int items = batch * kHeads;
+  const int* cu = p.cu;
+  if (batch < kTcCuCache) {
+    for (int i = tid; i <= batch; i += kTcThreads) sm.cu[i] = p.cu[i];
+    cu = sm.cu;
+  }
+  if (tid == 0) {
+    mbar_init(&sm.bar_s, 1);
+    mbar_init(&sm.bar_o, 1);
+    sm.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&sm.tmem, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem;  // S: columns [0, 128); O later reuses [0, 32)
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  volatile int* abort_flag = &sm.abort_flag;
+
+  constexpr uint32_t idesc_s = idesc_f16_f32(128, 128);              // Q K^T, both K-major
+  constexpr uint32_t idesc_o = idesc_f16_f32(128, 32) | (1u << 16);  // P V, B (V) MN-major
+
+  TcItem cur = tc_find(cu, batch, blockIdx.x, gridDim.x, items);
+  int bi = 0;
+  uint32_t ph = 0;
+  if (cur.item >= 0) {
+    tc_load(p, tokmask, cur, sm.buf[0], sm.keyok[0], tid);
+    cp_async_commit_tc();
+  }
+  while (cur.item >= 0) {
+    const TcItem nxt = tc_find(cu, batch, cur.item + gridDim.x, gridDim.x, items);
+    if (nxt.item >= 0) {
+      tc_load(p, tokmask, nxt, sm.buf[bi ^ 1], sm.keyok[bi ^ 1], tid);
+      cp_async_commit_tc();
+      cp_async_wait_tc<1>();
+    } else {
+      cp_async_wait_tc<0>();
+    }
+    fence_async_shared();  // this thread's cp.async data -> visible to the tensor core
+    __syncthreads();
+    TcBuf& B = sm.buf[bi];
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+        tc_mma_f16(tmem, sw64_kmajor_desc(smem_u32(B.q) + k * 32), sw64_kmajor_desc(smem_u32(B.k) + k * 32),
+                   idesc_s, k);
+      tc_commit(&sm.bar_s);
+    }
+
+    // ---- geometry of this tile (all warp-uniform except slot/q/row_ok)
+    const int len = cur.len;
+    const int lg = slot_log2(len);
+    const int Lp = 1 << lg;
+    const int G = kTcRows >> lg;
+    const int h0 = cur.h0;
+    const int nh = (kHeads - h0) < G ? (kHeads - h0) : G;
+    const int slot = tid >> lg, q = tid & (Lp - 1);
+    const bool row_ok = slot < nh && q < len;
+    const int s0 = (warp * 32) >> lg;  // slot of this warp's first row
+    const bool warp_active = Lp <= 16 ? (s0 < nh) : (s0 < nh && ((warp * 32) & (Lp - 1)) < len);
+    // TMEM columns this warp reads (its rows' slot keys) and how many 32-column chunks
+    const int c_lo = Lp <= 32 ? warp * 32 : s0 * Lp;
+    const int nchunk = Lp <= 32 ? 1 : (len + 31) >> 5;
+    const int off = slot * Lp - c_lo;  // my keys start at this column of the warp's range
+    // keys the O MMA contracts over
+    const int kused = Lp == kTcRows ? ((len + 15) & ~15) : nh * Lp;
+
+    if (!mbar_wait(&sm.bar_s, ph, abort_flag, nullptr)) break;
+    tc_fence_after();
+    const float scale = p.scale_log2;
+    float sum = 0.f;
+    if (warp_active) {
+      // Usable keys of chunk ch as a bit mask over its 32 columns: this row's keys are the
+      // columns [off, off + len) of the warp's range, further limited by the token mask.
+      auto chunk_mask = [&](int ch) -> uint32_t {
+        const int lo = max(off - ch * 32, 0), hi = min(off - ch * 32 + len, 32);
+        uint32_t m = 0;
+        if (hi > lo) m = (hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u)) & ~((1u << lo) - 1u);
+        if (tokmask) {
+          const uint32_t* kw = reinterpret_cast<const uint32_t*>(sm.keyok[bi] + c_lo + ch * 32);
+          uint32_t km = 0;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint32_t x = kw[i];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) km |= ((x >> (8 * e)) & 0xffu ? 1u : 0u) << (4 * i + e);
+          }
+          m &= km;
+        }
+        return m;
+      };
+      // pass 1: row max of the raw scores over this row's usable keys
+      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+      for (int ch = 0; ch < nchunk; ++ch) {
+        const uint32_t m = chunk_mask(ch);
+        float t[32];
+        tmem_ld32(tmem + lane_off + c_lo + ch * 32, t);
+        if (m == 0xffffffffu) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) mq[j & 3] = fmaxf(mq[j & 3], t[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) mq[j & 3] = fmaxf(mq[j & 3], (m >> j) & 1u ? t[j] : -INFINITY);
+        }
+      }
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      const float msc = mx == -INFINITY ? 0.f : mx * scale;
+      // pass 2: p = 2^(s * scale - max * scale), row sum, fp16 P row -> shared memory
+      float sq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int ch = 0; ch < nchunk; ++ch) {
+        const uint32_t m = row_ok ? chunk_mask(ch) : 0u;
+        float t[32];
+        tmem_ld32(tmem + lane_off + c_lo + ch * 32, t);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float e;
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(fmaf(t[j], scale, -msc)));
+          t[j] = e;
+        }
+        if (m != 0xffffffffu) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) t[j] = (m >> j) & 1u ? t[j] : 0.f;
+        }
+        uint32_t w[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          sq[j & 3] += t[j];
+          sq[(j + 1) & 3] += t[j + 1];
+          w[j >> 1] = pack_half2(t[j], t[j + 1]);
+        }
+        const int pc0 = (c_lo >> 3) + ch * 4;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          store_p_piece(sm, tid, pc0 + jj, make_uint4(w[4 * jj], w[4 * jj + 1], w[4 * jj + 2], w[4 * jj + 3]));
+      }
+      sum = (sq[0] + sq[1]) + (sq[2] + sq[3]);
+      // zero the pieces the O MMA reads that this row did not write
+      const int pc_lo = c_lo >> 3, pc_hi = pc_lo + nchunk * 4, pc_used = kused >> 3;
+#pragma unroll 1
+      for (int pc = 0; pc < 16; ++pc)
+        if (pc < pc_used && (pc < pc_lo || pc >= pc_hi)) store_p_piece(sm, tid, pc, make_uint4(0, 0, 0, 0));
+    }
+    fence_async_shared();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      for (int k = 0; k < (kused >> 4); ++k) {
+        const uint64_t adesc = sw128_kmajor_desc(smem_u32(sm.p[k >> 2]) + (k & 3) * 32);
+        const uint64_t bdesc = sw64_mnmajor_desc(smem_u32(B.v) + k * 1024);
+        tc_mma_f16(tmem, adesc, bdesc, idesc_o, k);
+      }
+      tc_commit(&sm.bar_o);
+    }
+    if (!mbar_wait(&sm.bar_o, ph, abort_flag, nullptr)) break;
+    tc_fence_after();
+    if (warp_active) {
+      float o[32];
+      tmem_ld32(tmem + lane_off, o);
+      if (row_ok) {
+        const float inv = sum > 0.f ? 1.0f / sum : 0.f;
+        __half* out = p.ctx + static_cast<size_t>(cur.start + q) * kHidden + (h0 + slot) * kHeadDim;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 w;
+          uint32_t* ww = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) ww[e] = pack_half2(o[j * 8 + 2 * e] * inv, o[j * 8 + 2 * e + 1] * inv);
+          *reinterpret_cast<uint4*>(out + j * 8) = w;
+        }
+      }
+    }
+    tc_fence_before();
+    ph ^= 1;
+    bi ^= 1;
+    cur = nxt;
+  }
+  cp_async_wait_tc<0>();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+int attention_tc_smem() { return static_cast<int>(sizeof(TcSmem)) + 4 * kTcCuCache + 1024; }
+
+cudaError_t launch_attention_tc(const AttnParams& p, int grid, cudaStream_t stream) {
+  const int smem = attention_tc_smem();
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  attention_tc_kernel<<<grid, kTcThreads, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace bbh

@@ -395,7 +395,12 @@ int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh
     }
     {
       KernelMark km(ws, s, 2);
-      BBH_CUDA(launch_attention(ap, attention_grid(ws->num_sms), s));
+      ap.min_len = 0;
+      BBH_CUDA(launch_attention_tc(ap, 2 * ws->num_sms, s));
+      if (ws->max_len > kAttnTcMaxLen) {
+        ap.min_len = kAttnTcMaxLen + 1;
+        BBH_CUDA(launch_attention(ap, attention_grid(ws->num_sms), s));
+      }
     }
     for (int j = 1; j < 4; ++j) {
       KernelMark km(ws, s, 2 + j);
@@ -630,7 +635,9 @@ int bbh_ws_kernel_times(bbh_ws* ws, double* ms, int64_t* counts) {
 }
 
 int bbh_launches_per_forward(const bbh_ws* ws) {
-  return ws && ws->w ? 2 + 5 * ws->w->layers : 0;
+  if (!ws || !ws->w) return 0;
+  const int per_layer = ws->max_len > bbh::kAttnTcMaxLen ? 6 : 5;
+  return 2 + per_layer * ws->w->layers;
 }
 
 int bbh_embed(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types, const int32_t* mask,
@@ -789,7 +796,11 @@ int bbh_attention_varlen(const uint16_t* qkv, uint16_t* ctx, const int32_t* cu_s
   ap.batch = batch;
   ap.max_len = max_len;
   ap.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(double(bbh::kHeadDim)));
-  BBH_CUDA(bbh::launch_attention(ap, bbh::attention_grid(g_num_sms(dev)), static_cast<cudaStream_t>(stream)));
+  BBH_CUDA(bbh::launch_attention_tc(ap, 2 * g_num_sms(dev), static_cast<cudaStream_t>(stream)));
+  if (max_len > bbh::kAttnTcMaxLen) {
+    ap.min_len = bbh::kAttnTcMaxLen + 1;
+    BBH_CUDA(bbh::launch_attention(ap, bbh::attention_grid(g_num_sms(dev)), static_cast<cudaStream_t>(stream)));
+  }
   return BBH_OK;
 }
 

@@ -32,6 +32,9 @@ enum DevErr : int {
 };
 
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // 4 s
+// try_wait suspends the waiting thread in hardware until the phase completes or this many
+// nanoseconds pass, so waiters do not spin on the issue slots the working warps need.
+constexpr unsigned int kSuspendHintNs = 1000000u;  // 1 ms
 
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
@@ -69,10 +72,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }

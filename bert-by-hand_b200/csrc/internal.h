@@ -85,10 +85,15 @@ struct AttnParams {
   const int32_t* meta;     // {B, T, max_len, has_mask}, or null to use the host values below
   int batch;
   int max_len;
+  int min_len;             // sentences shorter than this are skipped (the tcgen05 kernel has them)
   float scale_log2;        // log2(e) / sqrt(head_dim)
 };
+// mma.sync kernel: any length (used for sentences longer than kAttnTcMaxLen)
 cudaError_t launch_attention(const AttnParams& p, int grid, cudaStream_t stream);
 int attention_grid(int num_sms);
+// tcgen05 kernel: sentences of at most kAttnTcMaxLen tokens
+constexpr int kAttnTcMaxLen = 128;
+cudaError_t launch_attention_tc(const AttnParams& p, int grid, cudaStream_t stream);
 
 struct PoolParams {
   const __half* hidden;    // [T, 384]
