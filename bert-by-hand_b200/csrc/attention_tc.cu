@@ -9,14 +9,16 @@
 //      swizzled rows of 32 fp16; rows past the sentence are zero-filled), double buffered
 //      across tiles.
 //   2. One thread issues S = Q K^T (tcgen05.mma, M = N = 128, K = 32) into TMEM.
-//   3. Thread t owns query row t (TMEM lane t): it reads the columns of its own slot's keys
-//      (a key of another head, or past the sentence end, is dropped), takes the row max in
-//      a first pass over TMEM, then exponentiates in the exp2 domain, sums, and writes its
-//      row of P (fp16) to shared memory in the 128-byte swizzled K-major layout -- no warp
-//      shuffles, no S buffer in global memory. Warps whose 32 rows hold no query skip.
-//   4. One thread issues O = P V (tcgen05.mma, M = 128, N = 32, K = the keys in use, V as
-//      an MN-major operand) into the TMEM columns S used; thread t normalises its row by
-//      its softmax sum and stores the 32 head dimensions to the merged context [T, 384].
+//   3. Thread t owns query row t (TMEM lane t). Pass 1 reads the columns of its slot's keys
+//      and takes the row max (a key of another head, or past the sentence end, is dropped);
+//      pass 2 exponentiates in the exp2 domain, sums, and writes P as fp16 pairs back into
+//      the TMEM columns it has just read (P[k] at column k/2) -- no warp shuffles, no
+//      shared-memory or global copy of S or P. Warps whose 32 rows hold no query skip.
+//   4. One thread issues O = P V (tcgen05.mma with A = P read from TMEM, M = 128, N = 32,
+//      K = the keys in use, V as an MN-major shared-memory operand) into columns 64-95;
+//      thread t normalises its row by its softmax sum and stores the 32 head dimensions to
+//      the merged context [T, 384].
+// TMEM 128 columns, 48 KB shared memory and 128 registers per thread: four CTAs per SM.
 // A key is also dropped where the token mask is 0 (padded calls), as softmax.cu:43-59 does;
 // a row with no usable key gives zeros.
 #include "common.cuh"
@@ -37,7 +39,6 @@ static_assert(sizeof(TcBuf) % 1024 == 0, "swizzled operands must stay 1024-byte 
 
 struct TcSmem {
   TcBuf buf[2];
-  uint8_t p[2][kTcRows * 128];  // P, keys 0-63 and 64-127, 128-byte swizzle, K-major
   uint8_t keyok[2][kTcRows];    // 1 = usable key row (padded calls with a token mask)
   uint64_t bar_s, bar_o;
   uint32_t tmem;
@@ -136,11 +137,33 @@ __device__ __forceinline__ void tc_load(const AttnParams& p, const uint8_t* tokm
   }
 }
 
-__device__ __forceinline__ void store_p_piece(TcSmem& sm, int tid, int pc, uint4 w) {
-  *reinterpret_cast<uint4*>(sm.p[pc >> 3] + tid * 128 + (((pc & 7) ^ (tid & 7)) << 4)) = w;
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&w)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7]), "r"(w[8]), "r"(w[9]),
+      "r"(w[10]), "r"(w[11]), "r"(w[12]), "r"(w[13]), "r"(w[14]), "r"(w[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st8_zero(uint32_t taddr) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(0)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem]: A (K-major fp16 pairs, 8 columns per K=16 step) read
+// from tensor memory.
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
-__global__ void __launch_bounds__(kTcThreads, 2) attention_tc_kernel(AttnParams p) {
+__global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(AttnParams p) {
   extern __shared__ uint8_t tc_raw[];
   TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x;
@@ -164,7 +187,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) attention_tc_kernel(AttnParams 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = sm.tmem;  // S: columns [0, 128); O later reuses [0, 32)
+  const uint32_t tmem = sm.tmem;  // S: columns [0, 128); P (fp16 pairs) [0, 64); O [64, 96)
+  const uint32_t t_o = tmem + 64;
+  const int row = tid;
   const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
   volatile int* abort_flag = &sm.abort_flag;
 
@@ -206,11 +231,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) attention_tc_kernel(AttnParams 
     const int G = kTcRows >> lg;
     const int h0 = cur.h0;
     const int nh = (kHeads - h0) < G ? (kHeads - h0) : G;
-    const int slot = tid >> lg, q = tid & (Lp - 1);
+    const int slot = row >> lg, q = row & (Lp - 1);
     const bool row_ok = slot < nh && q < len;
     const int s0 = (warp * 32) >> lg;  // slot of this warp's first row
     const bool warp_active = Lp <= 16 ? (s0 < nh) : (s0 < nh && ((warp * 32) & (Lp - 1)) < len);
-    // TMEM columns this warp reads (its rows' slot keys) and how many 32-column chunks
+    // TMEM columns of the warp's rows' slot keys, in 32-column chunks
     const int c_lo = Lp <= 32 ? warp * 32 : s0 * Lp;
     const int nchunk = Lp <= 32 ? 1 : (len + 31) >> 5;
     const int off = slot * Lp - c_lo;  // my keys start at this column of the warp's range
@@ -220,34 +245,35 @@ __global__ void __launch_bounds__(kTcThreads, 2) attention_tc_kernel(AttnParams 
     if (!mbar_wait(&sm.bar_s, ph, abort_flag, nullptr)) break;
     tc_fence_after();
     const float scale = p.scale_log2;
+    // Usable keys of chunk ch as a bit mask over its 32 columns: this row's keys are the
+    // columns [off, off + len) of the warp's range, further limited by the token mask.
+    auto chunk_mask = [&](int ch) -> uint32_t {
+      const int lo = max(off - ch * 32, 0), hi = min(off - ch * 32 + len, 32);
+      uint32_t m = 0;
+      if (hi > lo) m = (hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u)) & ~((1u << lo) - 1u);
+      if (tokmask) {
+        const uint32_t* kw = reinterpret_cast<const uint32_t*>(sm.keyok[bi] + c_lo + ch * 32);
+        uint32_t km = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t x = kw[i];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) km |= ((x >> (8 * e)) & 0xffu ? 1u : 0u) << (4 * i + e);
+        }
+        m &= km;
+      }
+      return row_ok ? m : 0u;
+    };
     float sum = 0.f;
     if (warp_active) {
-      // Usable keys of chunk ch as a bit mask over its 32 columns: this row's keys are the
-      // columns [off, off + len) of the warp's range, further limited by the token mask.
-      auto chunk_mask = [&](int ch) -> uint32_t {
-        const int lo = max(off - ch * 32, 0), hi = min(off - ch * 32 + len, 32);
-        uint32_t m = 0;
-        if (hi > lo) m = (hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u)) & ~((1u << lo) - 1u);
-        if (tokmask) {
-          const uint32_t* kw = reinterpret_cast<const uint32_t*>(sm.keyok[bi] + c_lo + ch * 32);
-          uint32_t km = 0;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint32_t x = kw[i];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) km |= ((x >> (8 * e)) & 0xffu ? 1u : 0u) << (4 * i + e);
-          }
-          m &= km;
-        }
-        return m;
-      };
+      const uint32_t trow = tmem + lane_off;
       // pass 1: row max of the raw scores over this row's usable keys
       float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
       for (int ch = 0; ch < nchunk; ++ch) {
         const uint32_t m = chunk_mask(ch);
         float t[32];
-        tmem_ld32(tmem + lane_off + c_lo + ch * 32, t);
+        tmem_ld32(trow + c_lo + ch * 32, t);
         if (m == 0xffffffffu) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) mq[j & 3] = fmaxf(mq[j & 3], t[j]);
@@ -258,13 +284,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) attention_tc_kernel(AttnParams 
       }
       const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
       const float msc = mx == -INFINITY ? 0.f : mx * scale;
-      // pass 2: p = 2^(s * scale - max * scale), row sum, fp16 P row -> shared memory
+      // pass 2: p = 2^(s * scale - max * scale), row sum; P (fp16 pairs) overwrites the S
+      // columns already read: keys [32 ch, 32 ch + 32) of the range -> columns 16 ch .. +16
       float sq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
       for (int ch = 0; ch < nchunk; ++ch) {
-        const uint32_t m = row_ok ? chunk_mask(ch) : 0u;
+        const uint32_t m = chunk_mask(ch);
         float t[32];
-        tmem_ld32(tmem + lane_off + c_lo + ch * 32, t);
+        tmem_ld32(trow + c_lo + ch * 32, t);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           float e;
@@ -282,27 +309,24 @@ __global__ void __launch_bounds__(kTcThreads, 2) attention_tc_kernel(AttnParams 
           sq[(j + 1) & 3] += t[j + 1];
           w[j >> 1] = pack_half2(t[j], t[j + 1]);
         }
-        const int pc0 = (c_lo >> 3) + ch * 4;
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj)
-          store_p_piece(sm, tid, pc0 + jj, make_uint4(w[4 * jj], w[4 * jj + 1], w[4 * jj + 2], w[4 * jj + 3]));
+        tmem_st16(trow + (c_lo >> 1) + ch * 16, w);
       }
       sum = (sq[0] + sq[1]) + (sq[2] + sq[3]);
-      // zero the pieces the O MMA reads that this row did not write
-      const int pc_lo = c_lo >> 3, pc_hi = pc_lo + nchunk * 4, pc_used = kused >> 3;
+      // zeros in the P columns the O MMA reads outside this warp's key range (8 columns =
+      // 16 keys at a time; only this warp's own lanes are written)
+      const int z_lo = c_lo >> 4, z_hi = z_lo + nchunk * 2, z_used = kused >> 4;
 #pragma unroll 1
-      for (int pc = 0; pc < 16; ++pc)
-        if (pc < pc_used && (pc < pc_lo || pc >= pc_hi)) store_p_piece(sm, tid, pc, make_uint4(0, 0, 0, 0));
+      for (int z = 0; z < z_used; ++z)
+        if (z < z_lo || z >= z_hi) tmem_st8_zero(trow + z * 8);
+      tmem_wait_st();
     }
-    fence_async_shared();
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
       for (int k = 0; k < (kused >> 4); ++k) {
-        const uint64_t adesc = sw128_kmajor_desc(smem_u32(sm.p[k >> 2]) + (k & 3) * 32);
         const uint64_t bdesc = sw64_mnmajor_desc(smem_u32(B.v) + k * 1024);
-        tc_mma_f16(tmem, adesc, bdesc, idesc_o, k);
+        tc_mma_f16_ts(t_o, tmem + k * 8, bdesc, idesc_o, k);
       }
       tc_commit(&sm.bar_o);
     }
@@ -310,7 +334,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) attention_tc_kernel(AttnParams 
     tc_fence_after();
     if (warp_active) {
       float o[32];
-      tmem_ld32(tmem + lane_off, o);
+      tmem_ld32(t_o + lane_off, o);
       if (row_ok) {
         const float inv = sum > 0.f ? 1.0f / sum : 0.f;
         __half* out = p.ctx + static_cast<size_t>(cur.start + q) * kHidden + (h0 + slot) * kHeadDim;

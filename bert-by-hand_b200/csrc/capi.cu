@@ -396,7 +396,7 @@ int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh
     {
       KernelMark km(ws, s, 2);
       ap.min_len = 0;
-      BBH_CUDA(launch_attention_tc(ap, 2 * ws->num_sms, s));
+      BBH_CUDA(launch_attention_tc(ap, 4 * ws->num_sms, s));
       if (ws->max_len > kAttnTcMaxLen) {
         ap.min_len = kAttnTcMaxLen + 1;
         BBH_CUDA(launch_attention(ap, attention_grid(ws->num_sms), s));
@@ -796,7 +796,7 @@ int bbh_attention_varlen(const uint16_t* qkv, uint16_t* ctx, const int32_t* cu_s
   ap.batch = batch;
   ap.max_len = max_len;
   ap.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(double(bbh::kHeadDim)));
-  BBH_CUDA(bbh::launch_attention_tc(ap, 2 * g_num_sms(dev), static_cast<cudaStream_t>(stream)));
+  BBH_CUDA(bbh::launch_attention_tc(ap, 4 * g_num_sms(dev), static_cast<cudaStream_t>(stream)));
   if (max_len > bbh::kAttnTcMaxLen) {
     ap.min_len = bbh::kAttnTcMaxLen + 1;
     BBH_CUDA(bbh::launch_attention(ap, bbh::attention_grid(g_num_sms(dev)), static_cast<cudaStream_t>(stream)));
