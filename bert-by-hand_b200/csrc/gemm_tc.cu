@@ -40,9 +40,9 @@ struct GemmCfg {
   static constexpr int N_MMA = BN / MMA_N;
   static constexpr int TMA_B_ROWS = BN <= 256 ? BN : BN / 2;
   static constexpr int AUX_BYTES = 256 /*barriers*/ + 4 * kMaxBiasCols /*bias*/ + 8 * kHidden /*gamma, beta*/ +
-                                   2048 /*row statistics*/ + 2048 /*peer statistics*/;
+                                   4096 /*row statistics*/ + 2048 /*peer statistics*/;
   // epilogue warps: 4 TMEM lane quadrants x PARTS column parts
-  static constexpr int PARTS = (EPI != kEpiResLN && BN == 192) ? 3 : 2;
+  static constexpr int PARTS = BN == 192 ? 3 : 2;
   static constexpr int EPI_WARPS = 4 * PARTS;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int STAGING_BYTES = EPI_WARPS * 2 * 2048;  // per warp: 2 buffers x (32 rows x 64 B)
@@ -174,8 +174,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
   float* s_bias = reinterpret_cast<float*>(s_stage + Cfg::STAGING_BYTES + 256);  // [kMaxBiasCols]
   float* s_gamma = s_bias + kMaxBiasCols;                                            // [384]
   float* s_beta = s_gamma + kHidden;                                                 // [384]
-  float* red = s_beta + kHidden;  // [2 stats][2 halves][128 rows] (LayerNorm)
-  float2* xstat = reinterpret_cast<float2*>(red + 512);  // [2 slots][128 rows] peer (mean, M2)
+  float* red = s_beta + kHidden;  // [2 stats][PARTS][128 rows] (LayerNorm)
+  float2* xstat = reinterpret_cast<float2*>(red + 1024);  // [2 slots][128 rows] peer (mean, M2)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -308,13 +308,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
       const int c0 = tile_n0(tile) + half * HB;  // first output column of this warp
       const int row = m0 + rloc;
       const bool row_ok = row < rows;
-      uint4 rcur[4];
-      const __half* res_row = nullptr;
+      uint4 res[EPI == kEpiResLN ? HB / 8 : 1];
       if constexpr (EPI == kEpiResLN) {
-        res_row = p.residual + static_cast<size_t>(row_ok ? row : 0) * p.ldr + c0;
+        // this row's residual slice, fetched before the accumulator wait
+        const __half* res_row = p.residual + static_cast<size_t>(row_ok ? row : 0) * p.ldr + c0;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          rcur[j] = row_ok ? *(reinterpret_cast<const uint4*>(res_row) + j) : make_uint4(0, 0, 0, 0);
+        for (int j = 0; j < HB / 8; ++j)
+          res[j] = row_ok ? *(reinterpret_cast<const uint4*>(res_row) + j) : make_uint4(0, 0, 0, 0);
       }
       if (!mbar_wait(&accf_bar[acc], acc_phase, abort_flag, p.err)) break;
       tc_fence_after();
@@ -322,45 +322,39 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
       const int row0 = m0 + quad * 32;  // first row of this warp's 32-row slab
 
       if constexpr (EPI == kEpiResLN) {
-        // pass 1: v = acc + bias + residual (residual chunk c+1 is loaded while chunk c is
-        // processed; chunk 0 was fetched before the accumulator wait), written back to
-        // TMEM; shifted sums (shift = this warp's first value)
-        float shift = 0.f, s1 = 0.f, s2 = 0.f;
+        static_assert(HB == 64, "LayerNorm epilogue: 64 columns per warp");
+        // the accumulator slice, then hand the accumulator straight back to the MMA warp
+        float v[64];
+        tmem_ld64(tacc, tacc + 32, v);
+        tc_fence_before();
+        mbar_arrive(&acce_bar[acc]);
+        // v = acc + bias + residual; shifted sums (shift = this warp's first value)
+        ln_add32(v, s_bias + c0, &res[0]);
+        ln_add32(v + 32, s_bias + c0 + 32, &res[4]);
+        const float shift = v[0];
+        float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-        for (int c = 0; c < HB; c += 32) {
-          uint4 rnext[4];
-          if (c + 32 < HB) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              rnext[j] = row_ok ? *(reinterpret_cast<const uint4*>(res_row + c + 32) + j) : make_uint4(0, 0, 0, 0);
-          }
-          float v[32];
-          tmem_ld32(tacc + c, v);
-          ln_add32(v, s_bias + c0 + c, rcur);
-          if (c == 0) shift = v[0];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float d = v[j] - shift;
-            s1 += d;
-            s2 += d * d;
-          }
-          tmem_st32(tacc + c, *reinterpret_cast<float(*)[32]>(v));
-          if (c + 32 < HB) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) rcur[j] = rnext[j];
-          }
+        for (int j = 0; j < 64; ++j) {
+          const float d = v[j] - shift;
+          s1 += d;
+          s2 += d * d;
         }
-        // per-half mean and M2, combined with the partner warp (Chan et al. pairwise update)
-        const float mean_h = shift + s1 * (1.0f / HB);
-        const float m2_h = fmaxf(s2 - s1 * s1 * (1.0f / HB), 0.f);
-        red[half * 128 + rloc] = mean_h;
-        red[256 + half * 128 + rloc] = m2_h;
-        named_barrier(1 + quad, 64);
-        const float ma = red[rloc], mb = red[128 + rloc];
-        const float dm = ma - mb;
-        const float mean_c = 0.5f * (ma + mb);  // this CTA's 192 columns
-        const float m2_c = red[256 + rloc] + red[384 + rloc] + dm * dm * (0.25f * BN);
-        named_barrier(1 + quad, 64);  // partner done reading before the next tile overwrites
+        // per-part mean and M2 combined over the PARTS warps of this quadrant
+        // (Chan et al.: M2 = sum M2_i + n * sum (mean_i - mean)^2, equal part sizes n)
+        red[half * 128 + rloc] = shift + s1 * (1.0f / HB);
+        red[512 + half * 128 + rloc] = fmaxf(s2 - s1 * s1 * (1.0f / HB), 0.f);
+        named_barrier(1 + quad, 32 * Cfg::PARTS);
+        float mean_c = 0.f;
+#pragma unroll
+        for (int i = 0; i < Cfg::PARTS; ++i) mean_c += red[i * 128 + rloc];
+        mean_c *= 1.0f / Cfg::PARTS;
+        float m2_c = 0.f;
+#pragma unroll
+        for (int i = 0; i < Cfg::PARTS; ++i) {
+          const float d = red[i * 128 + rloc] - mean_c;
+          m2_c += red[512 + i * 128 + rloc] + d * d * HB;
+        }
+        named_barrier(1 + quad, 32 * Cfg::PARTS);  // all parts read before the next tile overwrites
         // exchange with the other CTA of the cluster (the other 192 columns)
         const int slot = iter & 1;
         if (half == 0) {
@@ -374,20 +368,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
         const float mean = 0.5f * (mean_c + ps.x);
         const float m2 = m2_c + ps.y + dp * dp * (0.5f * BN);
         const float rstd = rsqrtf(m2 * (1.0f / kHidden) + p.eps);
-        // pass 2: normalise, affine, store
-        int c = 0;
-#pragma unroll 1
-        for (; c + 64 <= HB; c += 64) {
-          float v[64];
-          tmem_ld64(tacc + c, tacc + c + 32, v);
-          ln_chunk(v, c0 + c, row0, cst, mean, rstd, s_gamma, s_beta);
-          ln_chunk(v + 32, c0 + c + 32, row0, cst, mean, rstd, s_gamma, s_beta);
-        }
-        if (c < HB) {
-          float v[32];
-          tmem_ld32(tacc + c, v);
-          ln_chunk(v, c0 + c, row0, cst, mean, rstd, s_gamma, s_beta);
-        }
+        // normalise, affine, store
+        ln_chunk(v, c0, row0, cst, mean, rstd, s_gamma, s_beta);
+        ln_chunk(v + 32, c0 + 32, row0, cst, mean, rstd, s_gamma, s_beta);
       } else {
         const float* sb = bias_in_smem ? s_bias : nullptr;
         int c = 0;
@@ -404,8 +387,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
           epi_chunk<EPI>(v, c0 + c, row0, cst, sb, p.bias, p.N);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&acce_bar[acc]);
+      if constexpr (EPI != kEpiResLN) {  // (the LayerNorm path released it after its load)
+        tc_fence_before();
+        mbar_arrive(&acce_bar[acc]);
+      }
       if (++acc == NACC) {
         acc = 0;
         acc_phase ^= 1;
