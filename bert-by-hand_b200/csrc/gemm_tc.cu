@@ -16,6 +16,7 @@
 //    fp32 (row statistics combined through shared memory), fp16 stores. Two TMEM accumulators (when 2*BN <= 512)
 //    let the MMA of tile i+1 overlap the epilogue of tile i.
 #include "common.cuh"
+#include "epilogue.cuh"
 #include "internal.h"
 #include "../../include/bbh.h"
 
@@ -24,7 +25,6 @@
 
 namespace bbh {
 
-constexpr int kMaxBiasCols = 2048;  // bias staged in shared memory when N <= this
 
 template <int BN, int EPI>
 struct GemmCfg {
@@ -45,7 +45,7 @@ struct GemmCfg {
   static constexpr int PARTS = BN == 192 ? 3 : 2;
   static constexpr int EPI_WARPS = 4 * PARTS;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  static constexpr int STAGING_BYTES = EPI_WARPS * 2 * 2048;  // per warp: 2 buffers x (32 rows x 64 B)
+  static constexpr int STAGING_BYTES = EPI_WARPS * 4096;  // per warp: 32 rows x 128 B
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align slack*/ + STAGING_BYTES + AUX_BYTES;
   static_assert(BN % 16 == 0 && MMA_N <= 256, "bad BN");
   static_assert(NACC * BN <= TMEM_COLS, "TMEM overflow");
@@ -56,76 +56,6 @@ struct GemmCfg {
 };
 
 
-// Output path of the epilogue: each warp owns 32 rows; a 32-column chunk of fp16 is
-// written to a per-warp staging buffer in the 64-byte-swizzle layout (16-byte piece c of
-// row r at piece c ^ ((r >> 1) & 3), so the 32 lanes' row writes hit distinct banks), then
-// lane 0 stores the 32 x 32 box with one TMA store. Two buffers per warp alternate; a
-// buffer is rewritten only after the store issued from it has finished reading it.
-struct ChunkStore {
-  uint8_t* buf;       // this warp's 2 x 2048 B
-  const CUtensorMap* map;
-  int lane;
-  int issued = 0;
-
-  __device__ __forceinline__ void put(const uint32_t (&w)[16], int col0, int row0) {
-    uint8_t* b = buf + (issued & 1) * 2048;
-    if (issued >= 2) {
-      if (lane == 0) bulk_wait_read<1>();
-      __syncwarp();
-    }
-    uint8_t* rowp = b + lane * 64;
-    const int sw = (lane >> 1) & 3;
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-      *reinterpret_cast<uint4*>(rowp + ((c ^ sw) << 4)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-    fence_async_shared();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(map, b, col0, row0);
-      bulk_commit();
-    }
-    ++issued;
-  }
-  __device__ __forceinline__ void drain() {
-    if (lane == 0) bulk_wait_all();
-    __syncwarp();
-  }
-};
-
-// Bias (+ GELU) on 32 accumulator columns, packed to fp16 and handed to the store path.
-// `bias` points at fp32 values in shared memory, or is null (then `gbias`, global fp16).
-template <int EPI>
-__device__ __forceinline__ void epi_chunk(const float* v, int col0, int row0, ChunkStore& st, const float* bias,
-                                          const __half* gbias, int N) {
-  uint32_t w[16];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int col = col0 + j * 8;
-    float b8[8];
-    if (bias) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) b8[e] = bias[col + e];
-    } else if (gbias && col + 8 <= N) {
-      unpack_half8(__ldg(reinterpret_cast<const uint4*>(gbias + col)), b8);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) b8[e] = 0.f;
-    }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float y0 = v[j * 8 + 2 * e] + b8[2 * e];
-      float y1 = v[j * 8 + 2 * e + 1] + b8[2 * e + 1];
-      if constexpr (EPI == kEpiGelu) {
-        y0 = gelu_fast(y0);
-        y1 = gelu_fast(y1);
-      }
-      w[j * 4 + e] = pack_half2(y0, y1);
-    }
-  }
-  st.put(w, col0, row0);
-}
-
-// v[0..32) += bias + residual (residual: 4 packed uint4 = 32 fp16).
 __device__ __forceinline__ void ln_add32(float* v, const float* bias, const uint4* res4) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -136,9 +66,8 @@ __device__ __forceinline__ void ln_add32(float* v, const float* bias, const uint
   }
 }
 
-__device__ __forceinline__ void ln_chunk(const float* v, int col0, int row0, ChunkStore& st, float mean, float rstd,
-                                         const float* gamma, const float* beta) {
-  uint32_t w[16];
+__device__ __forceinline__ void ln_pack32(const float* v, int col0, float mean, float rstd, const float* gamma,
+                                          const float* beta, uint32_t* w) {
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
     const int c = col0 + 2 * e;
@@ -146,7 +75,6 @@ __device__ __forceinline__ void ln_chunk(const float* v, int col0, int row0, Chu
     const float y1 = (v[2 * e + 1] - mean) * rstd * gamma[c + 1] + beta[c + 1];
     w[e] = pack_half2(y0, y1);
   }
-  st.put(w, col0, row0);
 }
 
 template <int BN, int EPI>
@@ -200,7 +128,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
     }
     for (int a = 0; a < NACC; ++a) {
       mbar_init(&accf_bar[a], 1);
-      mbar_init(&acce_bar[a], 32 * Cfg::EPI_WARPS);
+      mbar_init(&acce_bar[a], Cfg::EPI_WARPS);  // one arrival per epilogue warp
     }
     mbar_init(&xfull_bar[0], 128);
     mbar_init(&xfull_bar[1], 128);
@@ -326,8 +254,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
         // the accumulator slice, then hand the accumulator straight back to the MMA warp
         float v[64];
         tmem_ld64(tacc, tacc + 32, v);
-        tc_fence_before();
-        mbar_arrive(&acce_bar[acc]);
+        warp_arrive(&acce_bar[acc]);
         // v = acc + bias + residual; shifted sums (shift = this warp's first value)
         ln_add32(v, s_bias + c0, &res[0]);
         ln_add32(v + 32, s_bias + c0 + 32, &res[4]);
@@ -369,27 +296,23 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
         const float m2 = m2_c + ps.y + dp * dp * (0.5f * BN);
         const float rstd = rsqrtf(m2 * (1.0f / kHidden) + p.eps);
         // normalise, affine, store
-        ln_chunk(v, c0, row0, cst, mean, rstd, s_gamma, s_beta);
-        ln_chunk(v + 32, c0 + 32, row0, cst, mean, rstd, s_gamma, s_beta);
+        uint32_t w[32];
+        ln_pack32(v, c0, mean, rstd, s_gamma, s_beta, w);
+        ln_pack32(v + 32, c0 + 32, mean, rstd, s_gamma, s_beta, w + 16);
+        cst.put64(w, c0, row0);
       } else {
         const float* sb = bias_in_smem ? s_bias : nullptr;
-        int c = 0;
+        static_assert(HB % 64 == 0, "64-column output chunks");
 #pragma unroll 1
-        for (; c + 64 <= HB; c += 64) {
+        for (int c = 0; c < HB; c += 64) {
           float v[64];
           tmem_ld64(tacc + c, tacc + c + 32, v);
-          epi_chunk<EPI>(v, c0 + c, row0, cst, sb, p.bias, p.N);
-          epi_chunk<EPI>(v + 32, c0 + c + 32, row0, cst, sb, p.bias, p.N);
+          if (c + 64 >= HB) warp_arrive(&acce_bar[acc]);  // accumulator fully read
+          uint32_t w[32];
+          epi_pack32<EPI>(v, c0 + c, sb, p.bias, p.N, w);
+          epi_pack32<EPI>(v + 32, c0 + c + 32, sb, p.bias, p.N, w + 16);
+          cst.put64(w, c0 + c, row0);
         }
-        if (c < HB) {
-          float v[32];
-          tmem_ld32(tacc + c, v);
-          epi_chunk<EPI>(v, c0 + c, row0, cst, sb, p.bias, p.N);
-        }
-      }
-      if constexpr (EPI != kEpiResLN) {  // (the LayerNorm path released it after its load)
-        tc_fence_before();
-        mbar_arrive(&acce_bar[acc]);
       }
       if (++acc == NACC) {
         acc = 0;
@@ -517,18 +440,18 @@ int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const
     if (N != kHidden) return BBH_ERR_ARG;
     bn = 192;  // per CTA of a 2-CTA cluster
   } else if (N % 192 == 0) {
-    bn = 192;
+    bn = 192;  // three epilogue warps per TMEM quadrant
   } else if (N % 256 == 0) {
     bn = 256;
   } else {
     bn = 128;
   }
-  const int box_b = bn <= 256 ? bn : bn / 2;
+  const int box_b = bn;
   int rc = encode_2d(&plan->tmA, A, rows_cap, K, lda, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = encode_2d(&plan->tmB, W, N, K, K, 64, box_b, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_2d(&plan->tmC, C, rows_cap, N, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  rc = encode_2d(&plan->tmC, C, rows_cap, N, ldc, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   plan->bn = bn;
   plan->epi = epi;
@@ -548,10 +471,10 @@ int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const
 cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream) {
   switch (plan.epi * 1000 + plan.bn) {
     case kEpiBias * 1000 + 128: return launch_inst<128, kEpiBias>(plan, stream);
-    case kEpiBias * 1000 + 192: return launch_inst<192, kEpiBias>(plan, stream);
-    case kEpiBias * 1000 + 256: return launch_inst<256, kEpiBias>(plan, stream);
     case kEpiGelu * 1000 + 128: return launch_inst<128, kEpiGelu>(plan, stream);
+    case kEpiBias * 1000 + 192: return launch_inst<192, kEpiBias>(plan, stream);
     case kEpiGelu * 1000 + 192: return launch_inst<192, kEpiGelu>(plan, stream);
+    case kEpiBias * 1000 + 256: return launch_inst<256, kEpiBias>(plan, stream);
     case kEpiGelu * 1000 + 256: return launch_inst<256, kEpiGelu>(plan, stream);
     case kEpiResLN * 1000 + 192: return launch_inst<192, kEpiResLN>(plan, stream);
     default: return cudaErrorInvalidValue;
