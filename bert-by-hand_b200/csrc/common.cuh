@@ -368,26 +368,33 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
-
-// erf-GELU, x * Phi(x), evaluated as x - x / (1 + exp(2 y(x))) where y(x) approximates
-// atanh(erf(x / sqrt 2)) by an odd degree-9 polynomial on [-5.5, 5.5] (x clamped there).
-// The coefficients are this project's own weighted least-squares fit (tests/
-// test_gpu_kernels.py checks the result against erff); the 2*log2(e) factor of exp is
-// folded in so the exponential is one ex2. Max abs error vs exact GELU ~4e-6.
-__device__ __forceinline__ float gelu_fast(float x) {
-  constexpr float k = 2.0f * 1.4426950408889634f;
-  constexpr float a0 = 7.97853484e-01f * k, a1 = 3.64356497e-02f * k, a2 = -1.12335663e-04f * k,
-                  a3 = -3.22934132e-05f * k, a4 = 1.19315286e-06f * k;
-  const float xc = fminf(fmaxf(x, -5.5f), 5.5f);
-  const float x2 = xc * xc;
-  float p = fmaf(fmaf(fmaf(fmaf(a4, x2, a3), x2, a2), x2, a1), x2, a0);
-  p *= xc;
-  float e;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(p));
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(e + 1.0f));
-  return fmaf(-x, r, x);
+// erf-GELU, x * Phi(x) = x / 2 * (1 + tanh(y(x))), where y(x) = atanh(erf(x / sqrt 2))
+// is approximated by an odd degree-9 polynomial on [-5.5, 5.5] (x clamped there); the
+// coefficients are this project's own weighted least-squares fit,
+//   y(x) ~ x (0.797853484 + 3.64356497e-2 x^2 - 1.12335663e-4 x^4 - 3.22934132e-5 x^6
+//             + 1.19315286e-6 x^8).
+// It is evaluated on a pair of fp16 values (the GEMM output rounded to fp16, as the
+// reference's separate GELU pass sees it) in packed half2 arithmetic: the polynomial runs
+// in u = x^2 / 16 so that its fp16 coefficients stay normal and well scaled, and one
+// hardware tanh.approx.f16x2 serves both elements. Max abs error vs exact GELU ~1.5e-3
+// (under one fp16 ulp of the output); tests/test_gpu_kernels.py checks it against torch's
+// erf GELU and the reference's GELU golden vectors.
+__device__ __forceinline__ uint32_t gelu_half2(uint32_t xw) {
+  const __half2 x = *reinterpret_cast<const __half2*>(&xw);
+  const __half2 lim = __float2half2_rn(5.5f);
+  const __half2 xc = __hmin2(__hmax2(x, __hneg2(lim)), lim);
+  const __half2 u = __hmul2(__hmul2(xc, xc), __float2half2_rn(0.0625f));
+  __half2 z = __hfma2(__float2half2_rn(1.19315286e-06f * 65536.f), u, __float2half2_rn(-3.22934132e-05f * 4096.f));
+  z = __hfma2(z, u, __float2half2_rn(-1.12335663e-04f * 256.f));
+  z = __hfma2(z, u, __float2half2_rn(3.64356497e-02f * 16.f));
+  z = __hfma2(z, u, __float2half2_rn(7.97853484e-01f));
+  z = __hmul2(z, xc);
+  uint32_t zw = *reinterpret_cast<uint32_t*>(&z), tw;
+  asm("tanh.approx.f16x2 %0, %1;" : "=r"(tw) : "r"(zw));
+  const __half2 t = *reinterpret_cast<const __half2*>(&tw);
+  const __half2 hx = __hmul2(x, __float2half2_rn(0.5f));
+  const __half2 y = __hfma2(hx, t, hx);
+  return *reinterpret_cast<const uint32_t*>(&y);
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {

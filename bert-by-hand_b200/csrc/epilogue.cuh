@@ -54,8 +54,10 @@ __device__ __forceinline__ void epi_pack32(const float* v, int col0, const float
     const int col = col0 + j * 8;
     float b8[8];
     if (bias) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) b8[e] = bias[col + e];
+      const float4 lo = *reinterpret_cast<const float4*>(bias + col);
+      const float4 hi = *reinterpret_cast<const float4*>(bias + col + 4);
+      b8[0] = lo.x, b8[1] = lo.y, b8[2] = lo.z, b8[3] = lo.w;
+      b8[4] = hi.x, b8[5] = hi.y, b8[6] = hi.z, b8[7] = hi.w;
     } else if (gbias && col + 8 <= N) {
       unpack_half8(__ldg(reinterpret_cast<const uint4*>(gbias + col)), b8);
     } else {
@@ -64,13 +66,10 @@ __device__ __forceinline__ void epi_pack32(const float* v, int col0, const float
     }
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      float y0 = v[j * 8 + 2 * e] + b8[2 * e];
-      float y1 = v[j * 8 + 2 * e + 1] + b8[2 * e + 1];
-      if constexpr (EPI == kEpiGelu) {
-        y0 = gelu_fast(y0);
-        y1 = gelu_fast(y1);
-      }
+      const float y0 = v[j * 8 + 2 * e] + b8[2 * e];
+      const float y1 = v[j * 8 + 2 * e + 1] + b8[2 * e + 1];
       w[j * 4 + e] = pack_half2(y0, y1);
+      if constexpr (EPI == kEpiGelu) w[j * 4 + e] = gelu_half2(w[j * 4 + e]);
     }
   }
 }

@@ -25,6 +25,23 @@
 
 namespace bbh {
 
+// Optional wait-time accounting for tuning (compiled only with -DBBH_GEMM_TRACE):
+// [0] producer waiting for free ring slots, [1] MMA waiting for a free accumulator,
+// [2] MMA waiting for operands, [3] epilogue waiting for a finished accumulator (one warp),
+// [4] MMA-thread cycles from the first tile to the last commit, [5] tiles, [6] the same
+// span in globaltimer ns; clock64 units otherwise.
+#ifdef BBH_GEMM_TRACE
+__device__ unsigned long long g_gemm_trace[8];
+#define GEMM_TIMED(slot, expr)                   \
+  ([&] {                                         \
+    const long long t_ = clock64();              \
+    const bool r_ = (expr);                      \
+    trace_acc[slot] += clock64() - t_;           \
+    return r_;                                   \
+  }())
+#else
+#define GEMM_TIMED(slot, expr) (expr)
+#endif
 
 template <int BN, int EPI>
 struct GemmCfg {
@@ -107,6 +124,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+#ifdef BBH_GEMM_TRACE
+  long long trace_acc[7] = {};
+  const long long trace_t0 = clock64();
+  const unsigned long long trace_g0 = globaltimer();
+#endif
 
   const int rows = p.rows_dev ? *p.rows_dev : p.rows;
   const int m_tiles = (rows + Cfg::BM - 1) / Cfg::BM;
@@ -163,7 +185,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
         const int m0 = tile_m0(tile);
         const int n0 = tile_n0(tile);
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err)) break;
+          if (!GEMM_TIMED(0, mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err))) break;
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
           tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full_bar[stage], kb * Cfg::BK, m0);
 #pragma unroll
@@ -186,12 +208,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int tile = first_tile; tile < num_tiles && !*abort_flag; tile += tile_step) {
-        if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1, abort_flag, p.err)) break;
+        if (!GEMM_TIMED(1, mbar_wait(&acce_bar[acc], acc_phase ^ 1, abort_flag, p.err))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err)) {
+          if (!GEMM_TIMED(2, mbar_wait(&full_bar[stage], phase, abort_flag, p.err))) {
             ok = false;
             break;
           }
@@ -215,6 +237,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
         }
         if (!ok) break;
         tc_commit(&accf_bar[acc]);
+#ifdef BBH_GEMM_TRACE
+        trace_acc[4] = clock64() - trace_t0;
+        trace_acc[5] += 1;
+        trace_acc[6] = static_cast<long long>(globaltimer() - trace_g0);
+#endif
         if (++acc == NACC) {
           acc = 0;
           acc_phase ^= 1;
@@ -244,7 +271,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
         for (int j = 0; j < HB / 8; ++j)
           res[j] = row_ok ? *(reinterpret_cast<const uint4*>(res_row) + j) : make_uint4(0, 0, 0, 0);
       }
-      if (!mbar_wait(&accf_bar[acc], acc_phase, abort_flag, p.err)) break;
+      if (!GEMM_TIMED(3, mbar_wait(&accf_bar[acc], acc_phase, abort_flag, p.err))) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + lane_off + acc * BN + half * HB;
       const int row0 = m0 + quad * 32;  // first row of this warp's 32-row slab
@@ -322,6 +349,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
     cst.drain();
   }
 
+#ifdef BBH_GEMM_TRACE
+  if (lane == 0 && warp <= 2)
+    for (int i = 0; i < 7; ++i) atomicAdd(&g_gemm_trace[i], static_cast<unsigned long long>(trace_acc[i]));
+#endif
   tc_fence_before();
   __syncthreads();
   if (*abort_flag && warp == 0 && lane == 0) {
