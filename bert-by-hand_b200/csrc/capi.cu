@@ -317,13 +317,15 @@ int build_plans(bbh_ws* ws, const bbh_weights* w) {
     if (!rc) rc = make_gemm_plan(&P[1], ws->ctx, kHidden, T, L.o_w, kHidden, kHidden, ws->Y, kHidden, kEpiResLN, ws->num_sms);
     if (!rc) rc = make_gemm_plan(&P[2], ws->Y, kHidden, T, L.i_w, kFfn, kHidden, ws->inter, kFfn, kEpiGelu, ws->num_sms);
     if (!rc) rc = make_gemm_plan(&P[3], ws->inter, kFfn, T, L.o2_w, kHidden, kFfn, ws->X, kHidden, kEpiResLN, ws->num_sms);
+    if (!rc) rc = set_gemm_residual(&P[1], ws->X, kHidden);
+    if (!rc) rc = set_gemm_residual(&P[3], ws->Y, kHidden);
     if (rc) return fail(rc, "tensor map encoding failed");
     P[0].p.C = ws->qkv;  P[0].p.ldc = kQkvLd; P[0].p.bias = L.qkv_b;
     P[1].p.C = ws->Y;    P[1].p.ldc = kHidden; P[1].p.bias = L.o_b;
-    P[1].p.residual = ws->X; P[1].p.ldr = kHidden; P[1].p.gamma = L.ln1_g; P[1].p.beta = L.ln1_b;
+    P[1].p.gamma = L.ln1_g; P[1].p.beta = L.ln1_b;
     P[2].p.C = ws->inter; P[2].p.ldc = kFfn; P[2].p.bias = L.i_b;
     P[3].p.C = ws->X;    P[3].p.ldc = kHidden; P[3].p.bias = L.o2_b;
-    P[3].p.residual = ws->Y; P[3].p.ldr = kHidden; P[3].p.gamma = L.ln2_g; P[3].p.beta = L.ln2_b;
+    P[3].p.gamma = L.ln2_g; P[3].p.beta = L.ln2_b;
     for (int j = 0; j < 4; ++j) {
       P[j].p.rows_dev = ws->meta + 1;
       P[j].p.err = ws->err;
@@ -743,8 +745,10 @@ static int unit_gemm(const uint16_t* A, const uint16_t* W, const uint16_t* bias,
   plan.p.C = reinterpret_cast<__half*>(C);
   plan.p.ldc = N;
   plan.p.bias = reinterpret_cast<const __half*>(bias);
-  plan.p.residual = reinterpret_cast<const __half*>(residual);
-  plan.p.ldr = N;
+  if (epi == kEpiResLN) {
+    rc = set_gemm_residual(&plan, reinterpret_cast<const __half*>(residual), N);
+    if (rc) return fail(rc, "bbh_linear_residual_layernorm: residual tensor map encoding failed");
+  }
   plan.p.gamma = reinterpret_cast<const __half*>(gamma);
   plan.p.beta = reinterpret_cast<const __half*>(beta);
   plan.p.eps = eps;

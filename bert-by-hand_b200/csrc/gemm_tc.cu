@@ -21,6 +21,7 @@
 #include "../../include/bbh.h"
 
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 namespace bbh {
@@ -56,8 +57,12 @@ struct GemmCfg {
   static constexpr int MMA_N = BN <= 256 ? BN : BN / 2;
   static constexpr int N_MMA = BN / MMA_N;
   static constexpr int TMA_B_ROWS = BN <= 256 ? BN : BN / 2;
-  static constexpr int AUX_BYTES = 256 /*barriers*/ + 4 * kMaxBiasCols /*bias*/ + 8 * kHidden /*gamma, beta*/ +
-                                   4096 /*row statistics*/ + 2048 /*peer statistics*/;
+  static constexpr int BIAS_COLS = EPI == kEpiResLN ? kHidden : kMaxBiasCols;
+  static constexpr int AUX_BYTES = 256 /*barriers*/ + 4 * BIAS_COLS /*bias*/ +
+                                   (EPI == kEpiResLN ? 8 * kHidden /*gamma, beta*/ +
+                                                           2 * 2 * 3 * 128 * 4 /*row statistics, 2 slots*/ +
+                                                           2048 /*peer statistics*/
+                                                     : 0);
   // epilogue warps: 4 TMEM lane quadrants x PARTS column parts
   static constexpr int PARTS = BN == 192 ? 3 : 2;
   static constexpr int EPI_WARPS = 4 * PARTS;
@@ -65,6 +70,7 @@ struct GemmCfg {
   static constexpr int STAGING_BYTES = EPI_WARPS * 4096;  // per warp: 32 rows x 128 B
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align slack*/ + STAGING_BYTES + AUX_BYTES;
   static_assert(BN % 16 == 0 && MMA_N <= 256, "bad BN");
+  static_assert(SMEM <= 227 * 1024, "shared memory over the per-CTA limit");
   static_assert(NACC * BN <= TMEM_COLS, "TMEM overflow");
   // The LayerNorm epilogue runs on a 2-CTA cluster: each CTA owns half of the 384-wide row
   // and the two exchange per-row statistics through distributed shared memory.
@@ -97,7 +103,7 @@ __device__ __forceinline__ void ln_pack32(const float* v, int col0, float mean, 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, GemmParams p) {
   using Cfg = GemmCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int NACC = Cfg::NACC;
@@ -113,14 +119,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
   uint64_t* accf_bar = empty_bar + STAGES;
   uint64_t* acce_bar = accf_bar + NACC;
   uint64_t* xfull_bar = acce_bar + NACC;  // [2] peer statistics arrived (cluster LayerNorm)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xfull_bar + 2);
+  uint64_t* res_bar = xfull_bar + 2;      // [EPI_WARPS] residual slice landed in staging (LayerNorm)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(res_bar + Cfg::EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   uint8_t* s_stage = smem + STAGES * Cfg::STAGE_BYTES;  // epilogue staging, 1024-aligned
-  float* s_bias = reinterpret_cast<float*>(s_stage + Cfg::STAGING_BYTES + 256);  // [kMaxBiasCols]
-  float* s_gamma = s_bias + kMaxBiasCols;                                            // [384]
+  float* s_bias = reinterpret_cast<float*>(s_stage + Cfg::STAGING_BYTES + 256);  // [BIAS_COLS]
+  float* s_gamma = s_bias + Cfg::BIAS_COLS;                                          // [384]
   float* s_beta = s_gamma + kHidden;                                                 // [384]
-  float* red = s_beta + kHidden;  // [2 stats][PARTS][128 rows] (LayerNorm)
-  float2* xstat = reinterpret_cast<float2*>(red + 1024);  // [2 slots][128 rows] peer (mean, M2)
+  float* red = s_beta + kHidden;  // [2 slots][2 stats][3 parts][128 rows] (LayerNorm)
+  float2* xstat = reinterpret_cast<float2*>(red + 2 * 2 * 3 * 128);  // [2 slots][128 rows] peer (mean, M2)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -152,16 +159,18 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
       mbar_init(&accf_bar[a], 1);
       mbar_init(&acce_bar[a], Cfg::EPI_WARPS);  // one arrival per epilogue warp
     }
-    mbar_init(&xfull_bar[0], 128);
-    mbar_init(&xfull_bar[1], 128);
+    mbar_init(&xfull_bar[0], 4);  // one arrival per peer warp of column part 0
+    mbar_init(&xfull_bar[1], 4);
+    for (int w = 0; w < Cfg::EPI_WARPS; ++w) mbar_init(&res_bar[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmC);
+    if constexpr (EPI == kEpiResLN) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
-  const bool bias_in_smem = p.bias && p.N <= kMaxBiasCols;
+  const bool bias_in_smem = p.bias && p.N <= Cfg::BIAS_COLS;
   if (bias_in_smem)
     for (int i = threadIdx.x; i < p.N; i += blockDim.x) s_bias[i] = __half2float(p.bias[i]);
   if constexpr (EPI == kEpiResLN) {
@@ -258,19 +267,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int iter = 0;  // tiles processed by this CTA (peer-statistics slot and phase)
+    const int we = warp - 2;  // epilogue warp index
+    // LayerNorm: the warp's 32 x 64 residual slice of a tile is TMA-loaded into its staging
+    // buffer (the output chunk has the same shape and is written back in place), one tile
+    // ahead: the load for tile i+1 is issued as soon as tile i's store has read the buffer.
+    if constexpr (EPI == kEpiResLN) {
+      if (lane == 0 && first_tile < num_tiles) {
+        mbar_arrive_expect_tx(&res_bar[we], 4096);
+        tma_load_2d(cst.buf, &tmR, &res_bar[we], tile_n0(first_tile) + half * HB, tile_m0(first_tile) + quad * 32);
+      }
+    }
     for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++iter) {
       const int m0 = tile_m0(tile);
       const int c0 = tile_n0(tile) + half * HB;  // first output column of this warp
-      const int row = m0 + rloc;
-      const bool row_ok = row < rows;
-      uint4 res[EPI == kEpiResLN ? HB / 8 : 1];
-      if constexpr (EPI == kEpiResLN) {
-        // this row's residual slice, fetched before the accumulator wait
-        const __half* res_row = p.residual + static_cast<size_t>(row_ok ? row : 0) * p.ldr + c0;
-#pragma unroll
-        for (int j = 0; j < HB / 8; ++j)
-          res[j] = row_ok ? *(reinterpret_cast<const uint4*>(res_row) + j) : make_uint4(0, 0, 0, 0);
-      }
       if (!GEMM_TIMED(3, mbar_wait(&accf_bar[acc], acc_phase, abort_flag, p.err))) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + lane_off + acc * BN + half * HB;
@@ -282,6 +291,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
         float v[64];
         tmem_ld64(tacc, tacc + 32, v);
         warp_arrive(&acce_bar[acc]);
+        // the residual slice (swizzled rows in the staging buffer; lane = row)
+        if (!mbar_wait(&res_bar[we], iter & 1, abort_flag, p.err)) break;
+        uint8_t* rowp = cst.buf + lane * 128;
+        const int sw = lane & 7;
+        uint4 res[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) res[j] = *reinterpret_cast<const uint4*>(rowp + ((j ^ sw) << 4));
         // v = acc + bias + residual; shifted sums (shift = this warp's first value)
         ln_add32(v, s_bias + c0, &res[0]);
         ln_add32(v + 32, s_bias + c0 + 32, &res[4]);
@@ -294,27 +310,34 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
           s2 += d * d;
         }
         // per-part mean and M2 combined over the PARTS warps of this quadrant
-        // (Chan et al.: M2 = sum M2_i + n * sum (mean_i - mean)^2, equal part sizes n)
-        red[half * 128 + rloc] = shift + s1 * (1.0f / HB);
-        red[512 + half * 128 + rloc] = fmaxf(s2 - s1 * s1 * (1.0f / HB), 0.f);
+        // (Chan et al.: M2 = sum M2_i + n * sum (mean_i - mean)^2, equal part sizes n).
+        // Two scratch slots alternate by tile, so one barrier per tile suffices: a warp can
+        // rewrite a slot only after every part has passed the next tile's barrier.
+        const int slot = iter & 1;
+        float* rs = red + slot * (2 * 3 * 128);
+        rs[half * 128 + rloc] = shift + s1 * (1.0f / HB);
+        rs[384 + half * 128 + rloc] = fmaxf(s2 - s1 * s1 * (1.0f / HB), 0.f);
         named_barrier(1 + quad, 32 * Cfg::PARTS);
         float mean_c = 0.f;
 #pragma unroll
-        for (int i = 0; i < Cfg::PARTS; ++i) mean_c += red[i * 128 + rloc];
+        for (int i = 0; i < Cfg::PARTS; ++i) mean_c += rs[i * 128 + rloc];
         mean_c *= 1.0f / Cfg::PARTS;
         float m2_c = 0.f;
 #pragma unroll
         for (int i = 0; i < Cfg::PARTS; ++i) {
-          const float d = red[i * 128 + rloc] - mean_c;
-          m2_c += red[512 + i * 128 + rloc] + d * d * HB;
+          const float d = rs[i * 128 + rloc] - mean_c;
+          m2_c += rs[384 + i * 128 + rloc] + d * d * HB;
         }
-        named_barrier(1 + quad, 32 * Cfg::PARTS);  // all parts read before the next tile overwrites
-        // exchange with the other CTA of the cluster (the other 192 columns)
-        const int slot = iter & 1;
+        // exchange with the other CTA of the cluster (the other 192 columns): the lanes
+        // store, then one release arrival per warp
         if (half == 0) {
           const uint32_t peer = static_cast<uint32_t>(crank ^ 1);
           st_cluster_f32x2(mapa_shared(smem_u32(&xstat[slot * 128 + rloc]), peer), mean_c, m2_c);
-          mbar_arrive_remote(mapa_shared(smem_u32(&xfull_bar[slot]), peer));
+          __syncwarp();
+          if (lane == 0) {
+            fence_acq_rel_cluster();
+            mbar_arrive_remote(mapa_shared(smem_u32(&xfull_bar[slot]), peer));
+          }
         }
         if (!mbar_wait_cluster(&xfull_bar[slot], (iter >> 1) & 1, abort_flag, p.err)) break;
         const float2 ps = xstat[slot * 128 + rloc];
@@ -322,11 +345,25 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
         const float mean = 0.5f * (mean_c + ps.x);
         const float m2 = m2_c + ps.y + dp * dp * (0.5f * BN);
         const float rstd = rsqrtf(m2 * (1.0f / kHidden) + p.eps);
-        // normalise, affine, store
+        // normalise, affine, write the row back over its residual, store the chunk
         uint32_t w[32];
         ln_pack32(v, c0, mean, rstd, s_gamma, s_beta, w);
         ln_pack32(v + 32, c0 + 32, mean, rstd, s_gamma, s_beta, w + 16);
-        cst.put64(w, c0, row0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<uint4*>(rowp + ((j ^ sw) << 4)) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, cst.buf, c0, row0);
+          bulk_commit();
+          const int nt = tile + tile_step;
+          if (nt < num_tiles) {
+            bulk_wait_read<0>();
+            mbar_arrive_expect_tx(&res_bar[we], 4096);
+            tma_load_2d(cst.buf, &tmR, &res_bar[we], tile_n0(nt) + half * HB, tile_m0(nt) + quad * 32);
+          }
+        }
       } else {
         const float* sb = bias_in_smem ? s_bias : nullptr;
         static_assert(HB % 64 == 0, "64-column output chunks");
@@ -455,9 +492,9 @@ static cudaError_t launch_inst(const GemmPlan& plan, cudaStream_t stream) {
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, plan.tmA, plan.tmB, plan.tmC, plan.p);
+    return cudaLaunchKernelEx(&cfg, kern, plan.tmA, plan.tmB, plan.tmC, plan.tmR, plan.p);
   } else {
-    kern<<<plan.grid, Cfg::THREADS, Cfg::SMEM, stream>>>(plan.tmA, plan.tmB, plan.tmC, plan.p);
+    kern<<<plan.grid, Cfg::THREADS, Cfg::SMEM, stream>>>(plan.tmA, plan.tmB, plan.tmC, plan.tmR, plan.p);
     return cudaGetLastError();
   }
 }
@@ -478,6 +515,7 @@ int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const
     bn = 128;
   }
   const int box_b = bn;
+  memset(&plan->tmR, 0, sizeof(plan->tmR));
   int rc = encode_2d(&plan->tmA, A, rows_cap, K, lda, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = encode_2d(&plan->tmB, W, N, K, K, 64, box_b, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -499,7 +537,16 @@ int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const
   return BBH_OK;
 }
 
+int set_gemm_residual(GemmPlan* plan, const __half* R, int ldr) {
+  if (!plan || !R || ldr < plan->p.N) return BBH_ERR_ARG;
+  plan->p.residual = R;
+  plan->p.ldr = ldr;
+  // 32 x 64 boxes in the output chunks' 128-byte-swizzle layout
+  return encode_2d(&plan->tmR, R, plan->rows_cap, plan->p.N, ldr, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream) {
+  if (plan.epi == kEpiResLN && !plan.p.residual) return cudaErrorInvalidValue;
   switch (plan.epi * 1000 + plan.bn) {
     case kEpiBias * 1000 + 128: return launch_inst<128, kEpiBias>(plan, stream);
     case kEpiGelu * 1000 + 128: return launch_inst<128, kEpiGelu>(plan, stream);

@@ -35,6 +35,7 @@ struct GemmPlan {
   CUtensorMap tmA;
   CUtensorMap tmB;
   CUtensorMap tmC;
+  CUtensorMap tmR;  // residual (kEpiResLN), set by set_gemm_residual
   GemmParams p;
   int bn;
   int epi;
@@ -47,6 +48,8 @@ struct GemmPlan {
 // stride ldc (written by TMA stores, clipped at rows_cap and N). Returns 0 or a BBH_ERR_*.
 int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const __half* W, int N, int K,
                    __half* C, int ldc, int epi, int num_sms);
+// kEpiResLN: the residual [rows_cap, N] with row stride ldr (read with TMA, 16-byte aligned).
+int set_gemm_residual(GemmPlan* plan, const __half* R, int ldr);
 cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream);
 
 // ------------------------------------------------------------------ other kernels
