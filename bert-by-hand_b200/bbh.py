@@ -55,6 +55,8 @@ _SIGS = {
     "bbh_layernorm": (_I, [_P, _P, _P, _P, _I, _I, ctypes.c_float, _P, _P]),
     "bbh_attention_varlen": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bbh_mean_pool_l2": (_I, [_P, _P, _P, _I, _P, _P]),
+    "bbh_plan_batches": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, ctypes.POINTER(_I)]),
+    "bbh_embed_corpus": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _P, _P]),
     "bbh_embed_varlen_static": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P]),
     "bbh_static_device_error": (_I, []),
 }
@@ -234,6 +236,25 @@ class Workspace:
                                        B, T, max_len, _f16(out), _f16(dump), _stream(stream)))
         return (out, dump) if dump_layers else out
 
+    # ---- host corpus -------------------------------------------------------------------
+    def embed_corpus(self, ids, types, offsets, plan: "CorpusPlan", rank: int = 0, out=None, stream=None):
+        """Runs the plan's batches of `rank` from HOST numpy arrays (ids/types int32 of all
+        sentences back to back, offsets int64 [n+1]) with pipelined staging; returns the
+        fp16 [n, 384] host array with this rank's sentences filled in (corpus order)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        types = None if types is None else np.ascontiguousarray(types, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.int64)
+        n = offsets.size - 1
+        if out is None:
+            out = np.zeros((n, HIDDEN), dtype=np.float16)
+        if out.dtype != np.float16 or out.shape != (n, HIDDEN) or not out.flags.c_contiguous:
+            raise ValueError("out must be a contiguous float16 [n, 384] host array")
+        p = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+        _check(lib().bbh_embed_corpus(self.handle, self.weights.handle, p(ids), p(types), p(offsets), n,
+                                      p(plan.order), p(plan.batch_first), p(plan.batch_rank), plan.n_batches,
+                                      rank, p(out), _stream(stream)))
+        return out
+
     def free(self):
         if self.handle:
             lib().bbh_ws_free(self.handle)
@@ -244,6 +265,36 @@ class Workspace:
             self.free()
         except Exception:
             pass
+
+
+# ---- host corpus planning ---------------------------------------------------------------
+class CorpusPlan:
+    """bbh_plan_batches result: order [n] (corpus indices, length-sorted), batch b =
+    order[batch_first[b]:batch_first[b+1]], batch_rank [n_batches]."""
+
+    def __init__(self, order, batch_first, batch_rank, n_batches):
+        self.order, self.batch_first, self.batch_rank, self.n_batches = order, batch_first, batch_rank, n_batches
+
+    def batches(self, rank=None):
+        for b in range(self.n_batches):
+            if rank is None or self.batch_rank[b] == rank:
+                yield b, self.order[self.batch_first[b]:self.batch_first[b + 1]]
+
+
+def plan_batches(lengths, max_batch: int, max_tokens: int, world: int = 1) -> CorpusPlan:
+    """Length-sorted batches of at most max_batch sentences / max_tokens tokens, assigned to
+    `world` ranks by longest-processing-time on their FLOPs (host only, no GPU needed)."""
+    lengths = np.ascontiguousarray(lengths, dtype=np.int32)
+    n = lengths.size
+    order = np.empty(n, np.int32)
+    first = np.empty(n + 1, np.int32)
+    rank = np.empty(max(n, 1), np.int32)
+    nb = ctypes.c_int(0)
+    p = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    _check(lib().bbh_plan_batches(p(lengths), n, max_batch, max_tokens, world, p(order), p(first), p(rank),
+                                  ctypes.byref(nb)))
+    k = nb.value
+    return CorpusPlan(order, first[:k + 1].copy(), rank[:k].copy(), k)
 
 
 # ---- unit operators ---------------------------------------------------------------------

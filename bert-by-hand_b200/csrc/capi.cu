@@ -302,7 +302,24 @@ struct bbh_ws {
   std::vector<cudaEvent_t> ev;  // pairs
   std::vector<int> ev_kind;
   size_t ev_used = 0;
+  // host corpus driver staging (csrc/corpus.cu), created on first use
+  void* corpus_stage = nullptr;
+  void (*corpus_stage_free)(void*) = nullptr;
 };
+
+namespace bbh {
+int internal_fail(int code, const std::string& msg) { return fail(code, msg); }
+void ws_limits(const bbh_ws* ws, int* device, int* max_tokens, int* max_batch, int* max_len) {
+  *device = ws->device;
+  *max_tokens = ws->max_tokens;
+  *max_batch = ws->max_batch;
+  *max_len = ws->max_len;
+}
+void** ws_corpus_stage(bbh_ws* ws, void (*free_fn)(void*)) {
+  ws->corpus_stage_free = free_fn;
+  return &ws->corpus_stage;
+}
+}  // namespace bbh
 
 namespace {
 
@@ -590,6 +607,7 @@ void bbh_ws_free(bbh_ws* ws) {
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(ws->device);
+  if (ws->corpus_stage && ws->corpus_stage_free) ws->corpus_stage_free(ws->corpus_stage);
   drop_graph(ws);
   if (ws->cap_stream) cudaStreamDestroy(ws->cap_stream);
   for (auto e : ws->ev) cudaEventDestroy(e);

@@ -5,8 +5,20 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <string>
+
+struct bbh_ws;
 
 namespace bbh {
+
+// ------------------------------------------------------------------ C ABI internals
+// Sets the calling thread's bbh_last_error() message and returns code.
+int internal_fail(int code, const std::string& msg);
+// Device and capacity of a workspace.
+void ws_limits(const bbh_ws* ws, int* device, int* max_tokens, int* max_batch, int* max_len);
+// The workspace's slot for the corpus driver's staging state; free_fn releases it when
+// the workspace is freed.
+void** ws_corpus_stage(bbh_ws* ws, void (*free_fn)(void*));
 
 // ------------------------------------------------------------------ GEMM (tcgen05)
 enum Epilogue : int {

@@ -134,6 +134,33 @@ BBH_API int bbh_attention_varlen(const uint16_t* qkv, uint16_t* ctx, const int32
 BBH_API int bbh_mean_pool_l2(const uint16_t* hidden, const int32_t* cu_seqlens, const uint8_t* tokmask, int batch,
                      uint16_t* emb, void* stream);
 
+/* ---- host corpus driver --------------------------------------------------------------
+ * The reference's corpus loop (bench/corpus.cu:80-160) as a library call: sort the
+ * sentences by length, cut batches, run them, gather the embeddings back to corpus order.
+ *
+ * bbh_plan_batches (host only, no GPU needed): lengths [n] (host). Stable sort by
+ * length into order [n] (corpus indices); batches are consecutive runs of order[] with at
+ * most max_batch sentences and max_tokens tokens: batch b is order[batch_first[b] ..
+ * batch_first[b+1]), batch_first has room for n+1 entries. batch_rank [n] receives the
+ * rank of each batch for `world` ranks, by longest-processing-time first on each batch's
+ * FLOPs (sum over its sentences of 3,538,944 L + 1,536 L^2), so ranks finish together.
+ * *n_batches receives the batch count. A sentence longer than max_tokens or 512 returns
+ * BBH_ERR_CAPACITY. */
+BBH_API int bbh_plan_batches(const int32_t* lengths, int n, int max_batch, int max_tokens, int world, int32_t* order,
+                             int32_t* batch_first, int32_t* batch_rank, int* n_batches);
+/* bbh_embed_corpus: runs the batches of a plan that belong to `rank` and writes their
+ * sentences' embeddings into emb [n, 384] fp16 at their corpus rows (other rows are not
+ * touched). ids/types (types may be NULL = all 0) are HOST arrays of all sentences back
+ * to back, sentence i = [offsets[i], offsets[i+1]) (HOST int64 [n+1]); emb is HOST
+ * memory. Each batch is gathered into one of two pinned staging slots, copied to the
+ * device on a copy stream, embedded on `stream` (one graph replay), and copied back on a
+ * second copy stream, so the staging of one batch overlaps the forward of the previous
+ * one. Returns when every result is in emb. Batches must fit the workspace (checked on the
+ * host before anything runs); device-detected input errors return BBH_ERR_DEVICE. */
+BBH_API int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
+                             const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
+                             const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb, void* stream);
+
 /* ---- forward without device allocation ----------------------------------------------
  * No counterpart in the reference. Some callers cannot call cudaMalloc: hosts whose own
  * pool allocator owns all device memory and forbids allocations behind its back, and
