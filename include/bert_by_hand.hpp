@@ -18,6 +18,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <utility>
+#include <vector>
 
 #include "bbh.h"
 
@@ -116,4 +117,37 @@ inline void bert_embed_varlen(Workspace& ws, const ModelWeights& w, const int32_
   bbh_detail::check(bbh_embed_varlen(ws.get(w), w.handle, input_ids, token_type_ids, cu_seqlens, batch,
                                      total_tokens, max_len, reinterpret_cast<uint16_t*>(embedding), stream),
                     "bert_embed_varlen");
+}
+
+// Host corpus driver (the reference's bench/corpus.cu loop as a library call): plan
+// length-sorted batches once, then embed this rank's batches from host arrays into host
+// memory at corpus rows. Aborts on error like the calls above.
+struct CorpusPlan {
+  std::vector<int32_t> order, batch_first, batch_rank;
+  int n_batches = 0;
+};
+
+inline CorpusPlan plan_batches(const std::vector<int32_t>& lengths, int max_batch, int max_tokens, int world = 1) {
+  CorpusPlan p;
+  const int n = static_cast<int>(lengths.size());
+  p.order.resize(lengths.size());
+  p.batch_first.resize(lengths.size() + 1);
+  p.batch_rank.resize(lengths.size() + 1);
+  bbh_detail::check(bbh_plan_batches(lengths.data(), n, max_batch, max_tokens, world, p.order.data(),
+                                     p.batch_first.data(), p.batch_rank.data(), &p.n_batches),
+                    "plan_batches");
+  p.batch_first.resize(size_t(p.n_batches) + 1);
+  p.batch_rank.resize(size_t(p.n_batches));
+  return p;
+}
+
+// ids/types: host arrays of all sentences back to back (types may be null); offsets
+// [n+1] host; embedding: host [n, 384] fp16.
+inline void embed_corpus(Workspace& ws, const ModelWeights& w, const int32_t* ids, const int32_t* types,
+                         const int64_t* offsets, int n, const CorpusPlan& plan, __half* embedding, int rank = 0,
+                         cudaStream_t stream = nullptr) {
+  bbh_detail::check(bbh_embed_corpus(ws.get(w), w.handle, ids, types, offsets, n, plan.order.data(),
+                                     plan.batch_first.data(), plan.batch_rank.data(), plan.n_batches, rank,
+                                     reinterpret_cast<uint16_t*>(embedding), stream),
+                    "embed_corpus");
 }

@@ -134,3 +134,40 @@ def test_two_ranks_partition_the_corpus():
     assert set(np.unique(owners[owners >= 0]).tolist()) == {0, 1}
     # LPT keeps the two ranks' FLOPs within a few percent
     assert abs(works[0] - works[1]) / works.sum() < 0.05
+
+
+def test_cpp_dropin_plan_matches(tmp_path):
+    """bert_by_hand.hpp's plan_batches (C++ caller, linked against libbbh.so) gives the
+    same plan as the Python binding."""
+    import shutil
+    import subprocess
+
+    import bbh
+
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(nvcc):
+        pytest.skip("no nvcc")
+    src = tmp_path / "plan.cpp"
+    src.write_text(
+        '#include <cstdio>\n#include "bert_by_hand.hpp"\n'
+        "int main() {\n"
+        "  std::vector<int32_t> L;\n"
+        "  for (int i = 0; i < 300; ++i) L.push_back(5 + (i * 37) % 60);\n"
+        "  CorpusPlan p = plan_batches(L, 16, 400, 3);\n"
+        "  std::printf(\"%d\\n\", p.n_batches);\n"
+        "  for (int v : p.order) std::printf(\"%d \", v);\n  std::printf(\"\\n\");\n"
+        "  for (int v : p.batch_first) std::printf(\"%d \", v);\n  std::printf(\"\\n\");\n"
+        "  for (int v : p.batch_rank) std::printf(\"%d \", v);\n  std::printf(\"\\n\");\n"
+        "  return 0;\n}\n")
+    exe = tmp_path / "plan"
+    libdir = os.path.join(ROOT, "bert-by-hand_b200")
+    r = subprocess.run([nvcc, "-std=c++17", "-I" + os.path.join(ROOT, "include"), str(src), "-o", str(exe),
+                        "-L" + libdir, "-lbbh", "-Xlinker", "-rpath=" + libdir], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    lengths = np.array([5 + (i * 37) % 60 for i in range(300)], np.int32)
+    p = bbh.plan_batches(lengths, 16, 400, 3)
+    assert int(out[0]) == p.n_batches
+    assert [int(v) for v in out[1].split()] == p.order.tolist()
+    assert [int(v) for v in out[2].split()] == p.batch_first.tolist()
+    assert [int(v) for v in out[3].split()] == p.batch_rank.tolist()
