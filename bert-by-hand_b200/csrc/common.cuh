@@ -114,7 +114,15 @@ __device__ __forceinline__ void st_cluster_f32x2(uint32_t addr, float a, float b
   asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
 }
 
-__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+// Asynchronous store of two floats into another CTA's shared memory; the bytes count as
+// completed transaction bytes on that CTA's mbarrier (both given as shared::cluster
+// addresses), so the receiver needs no separate arrival from the sender.
+__device__ __forceinline__ void st_async_f32x2(uint32_t cluster_addr, float a, float b, uint32_t cluster_mbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                   cluster_addr),
+               "f"(a), "f"(b), "r"(cluster_mbar)
+               : "memory");
+}
 
 // Arrive (release, cluster scope) on an mbarrier given by its shared::cluster address.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {

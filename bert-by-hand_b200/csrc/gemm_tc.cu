@@ -92,11 +92,12 @@ __device__ __forceinline__ void ln_add32(float* v, const float* bias, const uint
 __device__ __forceinline__ void ln_pack32(const float* v, int col0, float mean, float rstd, const float* gamma,
                                           const float* beta, uint32_t* w) {
 #pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    const int c = col0 + 2 * e;
-    const float y0 = (v[2 * e] - mean) * rstd * gamma[c] + beta[c];
-    const float y1 = (v[2 * e + 1] - mean) * rstd * gamma[c + 1] + beta[c + 1];
-    w[e] = pack_half2(y0, y1);
+  for (int q = 0; q < 8; ++q) {
+    const float4 g = *reinterpret_cast<const float4*>(gamma + col0 + 4 * q);
+    const float4 b = *reinterpret_cast<const float4*>(beta + col0 + 4 * q);
+    const float* x = v + 4 * q;
+    w[2 * q] = pack_half2((x[0] - mean) * rstd * g.x + b.x, (x[1] - mean) * rstd * g.y + b.y);
+    w[2 * q + 1] = pack_half2((x[2] - mean) * rstd * g.z + b.z, (x[3] - mean) * rstd * g.w + b.w);
   }
 }
 
@@ -159,8 +160,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
       mbar_init(&accf_bar[a], 1);
       mbar_init(&acce_bar[a], Cfg::EPI_WARPS);  // one arrival per epilogue warp
     }
-    mbar_init(&xfull_bar[0], 4);  // one arrival per peer warp of column part 0
-    mbar_init(&xfull_bar[1], 4);
+    // peer statistics: one local arrival (with the expected byte count) + 128 rows x 8 B
+    // stored by the peer with st.async
+    mbar_init(&xfull_bar[0], 1);
+    mbar_init(&xfull_bar[1], 1);
     for (int w = 0; w < Cfg::EPI_WARPS; ++w) mbar_init(&res_bar[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -328,17 +331,17 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
           const float d = rs[i * 128 + rloc] - mean_c;
           m2_c += rs[384 + i * 128 + rloc] + d * d * HB;
         }
-        // exchange with the other CTA of the cluster (the other 192 columns): the lanes
-        // store, then one release arrival per warp
+        // exchange with the other CTA of the cluster (the other 192 columns): part-0 lanes
+        // send their row's (mean, M2) with st.async, which completes bytes on the peer's
+        // barrier; one thread per CTA posts the expected byte count on its own barrier.
+        // A slot is rewritten two tiles later, after every part of this quadrant has
+        // passed the next tile's barrier, so the receiver has read it by then.
         if (half == 0) {
           const uint32_t peer = static_cast<uint32_t>(crank ^ 1);
-          st_cluster_f32x2(mapa_shared(smem_u32(&xstat[slot * 128 + rloc]), peer), mean_c, m2_c);
-          __syncwarp();
-          if (lane == 0) {
-            fence_acq_rel_cluster();
-            mbar_arrive_remote(mapa_shared(smem_u32(&xfull_bar[slot]), peer));
-          }
+          st_async_f32x2(mapa_shared(smem_u32(&xstat[slot * 128 + rloc]), peer), mean_c, m2_c,
+                         mapa_shared(smem_u32(&xfull_bar[slot]), peer));
         }
+        if (we == 0 && lane == 0) mbar_arrive_expect_tx(&xfull_bar[slot], 128 * 8);
         if (!mbar_wait_cluster(&xfull_bar[slot], (iter >> 1) & 1, abort_flag, p.err)) break;
         const float2 ps = xstat[slot * 128 + rloc];
         const float dp = mean_c - ps.x;
