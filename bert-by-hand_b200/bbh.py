@@ -57,6 +57,8 @@ _SIGS = {
     "bbh_mean_pool_l2": (_I, [_P, _P, _P, _I, _P, _P]),
     "bbh_plan_batches": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, ctypes.POINTER(_I)]),
     "bbh_embed_corpus": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _P, _P]),
+    "bbh_pair_similarity": (_I, [_P, _I, _P, _I, _P, _P]),
+    "bbh_spearman": (_I, [_P, _P, _I, ctypes.POINTER(ctypes.c_double)]),
     "bbh_embed_varlen_static": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P]),
     "bbh_static_device_error": (_I, []),
 }
@@ -295,6 +297,29 @@ def plan_batches(lengths, max_batch: int, max_tokens: int, world: int = 1) -> Co
                                   ctypes.byref(nb)))
     k = nb.value
     return CorpusPlan(order, first[:k + 1].copy(), rank[:k].copy(), k)
+
+
+# ---- similarity evaluation (the step after the path) ---------------------------------------
+def pair_similarity(emb, pairs, stream=None):
+    """emb fp16 [n, 384], pairs int32 [m, 2] (CUDA tensors) -> fp32 [m] dot products."""
+    if pairs.dtype != torch.int32 or pairs.dim() != 2 or pairs.shape[1] != 2:
+        raise ValueError("pairs must be int32 [m, 2]")
+    sims = torch.empty(pairs.shape[0], dtype=torch.float32, device=emb.device)
+    _check(lib().bbh_pair_similarity(_f16(emb), emb.shape[0], _ptr(pairs), pairs.shape[0], _ptr(sims),
+                                     _stream(stream)))
+    return sims
+
+
+def spearman(x, y) -> float:
+    """Spearman rank correlation of two host sequences (average ranks for ties)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.ascontiguousarray(y, dtype=np.float32)
+    if x.shape != y.shape:
+        raise ValueError("x and y differ in length")
+    rho = ctypes.c_double(0.0)
+    _check(lib().bbh_spearman(x.ctypes.data_as(ctypes.c_void_p), y.ctypes.data_as(ctypes.c_void_p), x.size,
+                              ctypes.byref(rho)))
+    return rho.value
 
 
 # ---- unit operators ---------------------------------------------------------------------

@@ -161,6 +161,17 @@ BBH_API int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* id
                              const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
                              const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb, void* stream);
 
+/* ---- the step after the path: similarity evaluation -----------------------------------
+ * scripts/benchmark.py:54-61 of the reference: sims = einsum("ij,ij->i", embs[a], embs[b])
+ * over sentence pairs, then scipy's spearmanr against gold scores.
+ * bbh_pair_similarity: emb [n, 384] fp16 (device, 16-byte aligned), pairs [m, 2] int32
+ * (device) -> sims [m] fp32 (device), dot products in fp32 (the cosine for unit
+ * embeddings). A pair with an index outside [0, n) gives NaN. Asynchronous on stream.
+ * bbh_spearman (host only): Spearman rank correlation of x and y [n] (ties get average
+ * ranks, as scipy.stats.spearmanr); n >= 2, no NaN. */
+BBH_API int bbh_pair_similarity(const uint16_t* emb, int n, const int32_t* pairs, int m, float* sims, void* stream);
+BBH_API int bbh_spearman(const float* x, const float* y, int n, double* rho);
+
 /* ---- forward without device allocation ----------------------------------------------
  * No counterpart in the reference. Some callers cannot call cudaMalloc: hosts whose own
  * pool allocator owns all device memory and forbids allocations behind its back, and
