@@ -37,6 +37,9 @@ _SIGS = {
     "bbh_tensor_numel": (ctypes.c_int64, [_I, _I]),
     "bbh_weights_load": (_I, [ctypes.c_char_p, _I, _I, ctypes.POINTER(_P)]),
     "bbh_weights_from_host": (_I, [ctypes.POINTER(_P), _I, _I, ctypes.POINTER(_P)]),
+    "bbh_weights_pack": (_I, [ctypes.c_char_p, _I, ctypes.c_char_p]),
+    "bbh_blob_check": (_I, [ctypes.c_char_p, ctypes.POINTER(_I)]),
+    "bbh_weights_load_blob": (_I, [ctypes.c_char_p, _I, ctypes.POINTER(_P)]),
     "bbh_weights_free": (None, [_P]),
     "bbh_weights_layers": (_I, [_P]),
     "bbh_ws_create": (_I, [_P, _I, _I, _I, ctypes.POINTER(_P)]),
@@ -144,6 +147,13 @@ class ModelWeights:
         h = _P()
         _check(lib().bbh_weights_load(directory.encode(), layers, device, ctypes.byref(h)))
         return cls(h, layers, device)
+
+    @classmethod
+    def load_blob(cls, path: str, device: int = 0) -> "ModelWeights":
+        """One-file weights written by pack_weights()."""
+        h = _P()
+        _check(lib().bbh_weights_load_blob(path.encode(), device, ctypes.byref(h)))
+        return cls(h, lib().bbh_weights_layers(h), device)
 
     @classmethod
     def from_numpy(cls, weights: dict, layers: int = 6, device: int = 0) -> "ModelWeights":
@@ -267,6 +277,19 @@ class Workspace:
             self.free()
         except Exception:
             pass
+
+
+# ---- weight blob (host only) ---------------------------------------------------------------
+def pack_weights(directory: str, layers: int, path: str) -> None:
+    """<directory>/<HF key>.bin per-tensor files -> one checked blob file."""
+    _check(lib().bbh_weights_pack(directory.encode(), layers, path.encode()))
+
+
+def blob_check(path: str) -> int:
+    """Validates a weight blob; returns its layer count (raises BBHError on corruption)."""
+    n = ctypes.c_int(0)
+    _check(lib().bbh_blob_check(path.encode(), ctypes.byref(n)))
+    return n.value
 
 
 # ---- host corpus planning ---------------------------------------------------------------

@@ -59,6 +59,17 @@ BBH_API int64_t bbh_tensor_numel(int layers, int index);
 BBH_API int bbh_weights_load(const char* dir, int layers, int device, bbh_weights** out);
 /* tensors[i] = host pointer to tensor i (fp16 bits) in bbh_tensor_name() order. */
 BBH_API int bbh_weights_from_host(const uint16_t* const* tensors, int layers, int device, bbh_weights** out);
+/* Single-file weight blob (no counterpart in the reference, which opens one file per
+ * tensor): bbh_weights_pack (host only) reads <dir>/<key>.bin for every tensor of the
+ * catalogue and writes one file -- header "BBHW", version, layer and tensor counts, data
+ * offset/size and an FNV-1a 64 checksum, a table of (name, numel, offset), then the fp16
+ * tensors 256-byte aligned. bbh_blob_check (host only) validates a blob (magic, version,
+ * names and sizes against the catalogue, bounds, checksum) and returns its layer count;
+ * bbh_weights_load_blob loads it into a device arena with one read (BBH_ERR_IO on any
+ * mismatch or corruption). */
+BBH_API int bbh_weights_pack(const char* dir, int layers, const char* blob_path);
+BBH_API int bbh_blob_check(const char* blob_path, int* layers);
+BBH_API int bbh_weights_load_blob(const char* blob_path, int device, bbh_weights** out);
 BBH_API void bbh_weights_free(bbh_weights* w);
 BBH_API int bbh_weights_layers(const bbh_weights* w);
 

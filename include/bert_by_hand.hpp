@@ -70,6 +70,13 @@ inline ModelWeights load_model_weights(const char* dir = model::WEIGHTS_DIR, int
   return ModelWeights(w);
 }
 
+// The same weights from one blob file (bbh_weights_pack of a weights/ folder).
+inline ModelWeights load_model_weights_blob(const char* path, int device = 0) {
+  bbh_weights* w = nullptr;
+  bbh_detail::check(bbh_weights_load_blob(path, device, &w), "load_model_weights_blob");
+  return ModelWeights(w);
+}
+
 // Scratch sized once for batch x seq tokens. The device buffers are created on the first
 // forward (they are tied to the weights' device and GEMM descriptors).
 struct Workspace {
