@@ -60,6 +60,10 @@ _SIGS = {
     "bbh_mean_pool_l2": (_I, [_P, _P, _P, _I, _P, _P]),
     "bbh_plan_batches": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, ctypes.POINTER(_I)]),
     "bbh_embed_corpus": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _P, _P]),
+    "bbh_vocab_load": (_I, [ctypes.c_char_p, _I, ctypes.POINTER(_P)]),
+    "bbh_vocab_free": (None, [_P]),
+    "bbh_vocab_size": (_I, [_P]),
+    "bbh_tokenize": (_I, [_P, _P, _I, _I, _P, ctypes.c_int64, _P, ctypes.POINTER(ctypes.c_int64)]),
     "bbh_pair_similarity": (_I, [_P, _I, _P, _I, _P, _P]),
     "bbh_spearman": (_I, [_P, _P, _I, ctypes.POINTER(ctypes.c_double)]),
     "bbh_embed_varlen_static": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P]),
@@ -270,6 +274,48 @@ class Workspace:
     def free(self):
         if self.handle:
             lib().bbh_ws_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+# ---- WordPiece tokenizer (host only) --------------------------------------------------------
+class Vocab:
+    """BERT vocab.txt + WordPiece tokenization into the packed (ids, cu_seqlens) layout."""
+
+    def __init__(self, path: str, lowercase: bool = True):
+        self.handle = _P()
+        _check(lib().bbh_vocab_load(path.encode(), 1 if lowercase else 0, ctypes.byref(self.handle)))
+
+    def __len__(self):
+        return lib().bbh_vocab_size(self.handle)
+
+    def tokenize(self, texts, max_len: int = 128):
+        """-> (ids int32 [total], cu_seqlens int32 [n+1]) for a list of str."""
+        enc = [t.encode("utf-8") for t in texts]
+        arr = (ctypes.c_char_p * max(len(enc), 1))(*enc)
+        cu = np.zeros(len(enc) + 1, np.int32)
+        total = ctypes.c_int64(0)
+        cap = sum(min(len(e), 4 * max_len) for e in enc) + 2 * len(enc) + 16
+        for _ in range(2):
+            ids = np.empty(max(cap, 1), np.int32)
+            rc = lib().bbh_tokenize(self.handle, ctypes.cast(arr, ctypes.c_void_p), len(enc), max_len,
+                                    ids.ctypes.data_as(ctypes.c_void_p), cap, cu.ctypes.data_as(ctypes.c_void_p),
+                                    ctypes.byref(total))
+            if rc == BBH_OK:
+                return ids[:total.value].copy(), cu
+            if rc != -2:
+                _check(rc)
+            cap = total.value
+        _check(rc)
+
+    def free(self):
+        if self.handle:
+            lib().bbh_vocab_free(self.handle)
             self.handle = None
 
     def __del__(self):

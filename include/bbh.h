@@ -172,6 +172,23 @@ BBH_API int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* id
                              const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
                              const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb, void* stream);
 
+/* ---- the step before the path: WordPiece tokenizer (host only) ---------------------------
+ * The reference tokenizes with the HF tokenizer of its sentence-transformers model
+ * (scripts/dump_corpus.py:34-38: BERT uncased, truncation=True, max_length=128) and has no
+ * tokenizer of its own. bbh_vocab_load reads a BERT vocab.txt (one token per line, id =
+ * line number; must contain [UNK], [CLS], [SEP]); lowercase = 1 for uncased models (also
+ * strips accents). bbh_tokenize turns n UTF-8 texts into the packed layout of
+ * bbh_embed_varlen: ids[total] = [CLS] pieces [SEP] per text, each text truncated to
+ * max_len tokens including the two specials, cu_seqlens[n+1] offsets (host arrays).
+ * *total receives the number of ids; if it exceeds ids_cap nothing past ids_cap is written
+ * and BBH_ERR_CAPACITY is returned (call again with a larger buffer). */
+typedef struct bbh_vocab bbh_vocab;
+BBH_API int bbh_vocab_load(const char* vocab_path, int lowercase, bbh_vocab** out);
+BBH_API void bbh_vocab_free(bbh_vocab* v);
+BBH_API int bbh_vocab_size(const bbh_vocab* v);
+BBH_API int bbh_tokenize(const bbh_vocab* v, const char* const* texts, int n, int max_len, int32_t* ids,
+                         int64_t ids_cap, int32_t* cu_seqlens, int64_t* total);
+
 /* ---- the step after the path: similarity evaluation -----------------------------------
  * scripts/benchmark.py:54-61 of the reference: sims = einsum("ij,ij->i", embs[a], embs[b])
  * over sentence pairs, then scipy's spearmanr against gold scores.

@@ -17,6 +17,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <string>
 #include <utility>
 #include <vector>
 
@@ -158,3 +159,43 @@ inline void embed_corpus(Workspace& ws, const ModelWeights& w, const int32_t* id
                                      reinterpret_cast<uint16_t*>(embedding), stream),
                     "embed_corpus");
 }
+
+// WordPiece tokenization into the packed layout of bert_embed_varlen (host vectors).
+struct Tokenized {
+  std::vector<int32_t> ids, cu_seqlens;
+};
+
+class Vocabulary {
+ public:
+  explicit Vocabulary(const char* vocab_txt, bool lowercase = true) {
+    bbh_detail::check(bbh_vocab_load(vocab_txt, lowercase ? 1 : 0, &v_), "Vocabulary");
+  }
+  Vocabulary(const Vocabulary&) = delete;
+  Vocabulary& operator=(const Vocabulary&) = delete;
+  ~Vocabulary() { bbh_vocab_free(v_); }
+
+  Tokenized tokenize(const std::vector<std::string>& texts, int max_len = model::SEQ_LEN) const {
+    std::vector<const char*> p(texts.size());
+    size_t cap = 16;
+    for (size_t i = 0; i < texts.size(); ++i) {
+      p[i] = texts[i].c_str();
+      cap += texts[i].size() + 2;
+    }
+    Tokenized t;
+    t.cu_seqlens.resize(texts.size() + 1);
+    int64_t total = 0;
+    for (int attempt = 0; attempt < 2; ++attempt) {
+      t.ids.resize(cap);
+      const int rc = bbh_tokenize(v_, p.data(), static_cast<int>(texts.size()), max_len, t.ids.data(),
+                                  static_cast<int64_t>(cap), t.cu_seqlens.data(), &total);
+      if (rc == BBH_OK) break;
+      if (rc != BBH_ERR_CAPACITY || attempt) bbh_detail::check(rc, "tokenize");
+      cap = static_cast<size_t>(total);
+    }
+    t.ids.resize(static_cast<size_t>(total));
+    return t;
+  }
+
+ private:
+  bbh_vocab* v_ = nullptr;
+};
