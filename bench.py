@@ -47,7 +47,7 @@ WORKLOADS = {
 
 # GEMM shapes per token and layer, by kernel kind: (N, K)
 GEMM_NK = {"qkv_gemm": (1152, 384), "o_gemm_ln": (384, 384), "ffn1_gemm_gelu": (1536, 384),
-           "ffn2_gemm_ln": (384, 1536)}
+           "ffn2_gemm_ln": (384, 1536), "ffn_fused": (1536, 2 * 384)}  # fused: both FFN GEMMs
 # algorithmic HBM bytes per token for the memory-bound kernels
 MEM_BYTES = {"embed_ln": 8 + 768 + 768, "pool_l2": 768, "attention": 4 * 768}
 

@@ -45,6 +45,7 @@ _SIGS = {
     "bbh_ws_create": (_I, [_P, _I, _I, _I, ctypes.POINTER(_P)]),
     "bbh_ws_free": (None, [_P]),
     "bbh_ws_set_graph": (_I, [_P, _I]),
+    "bbh_ws_set_ffn_fusion": (_I, [_P, _I]),
     "bbh_device_error": (_I, [_P, _I]),
     "bbh_launches_per_forward": (_I, [_P]),
     "bbh_ws_set_kernel_timing": (_I, [_P, _I]),
@@ -56,6 +57,7 @@ _SIGS = {
     "bbh_linear": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "bbh_linear_residual_layernorm": (_I, [_P, _P, _P, _P, _P, _P, ctypes.c_float, _P, _I, _I, _P]),
     "bbh_layernorm": (_I, [_P, _P, _P, _P, _I, _I, ctypes.c_float, _P, _P]),
+    "bbh_ffn_block": (_I, [_P, _P, _P, _P, _P, _P, _P, ctypes.c_float, _P, _I, _P]),
     "bbh_attention_varlen": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bbh_mean_pool_l2": (_I, [_P, _P, _P, _I, _P, _P]),
     "bbh_plan_batches": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, ctypes.POINTER(_I)]),
@@ -195,15 +197,19 @@ class Workspace:
     def set_graph(self, enable: bool):
         _check(lib().bbh_ws_set_graph(self.handle, 1 if enable else 0))
 
-    KERNEL_KINDS = ("embed_ln", "qkv_gemm", "attention", "o_gemm_ln", "ffn1_gemm_gelu", "ffn2_gemm_ln", "pool_l2")
+    def set_ffn_fusion(self, enable: bool):
+        _check(lib().bbh_ws_set_ffn_fusion(self.handle, 1 if enable else 0))
+
+    KERNEL_KINDS = ("embed_ln", "qkv_gemm", "attention", "o_gemm_ln", "ffn1_gemm_gelu", "ffn2_gemm_ln", "pool_l2",
+                    "ffn_fused")
 
     def set_kernel_timing(self, enable: bool):
         _check(lib().bbh_ws_set_kernel_timing(self.handle, 1 if enable else 0))
 
     def kernel_times(self) -> dict:
         """{kind: (total ms, launches)} since the last call (synchronises)."""
-        ms = (ctypes.c_double * 7)()
-        n = (ctypes.c_int64 * 7)()
+        ms = (ctypes.c_double * len(self.KERNEL_KINDS))()
+        n = (ctypes.c_int64 * len(self.KERNEL_KINDS))()
         _check(lib().bbh_ws_kernel_times(self.handle, ms, n))
         return {k: (ms[i], n[i]) for i, k in enumerate(self.KERNEL_KINDS)}
 
@@ -407,6 +413,14 @@ def linear_residual_layernorm(A, W, bias, residual, gamma, beta, eps=1e-12, stre
     _check(lib().bbh_linear_residual_layernorm(_f16(A), _f16(W), _f16(bias), _f16(residual), _f16(gamma),
                                                _f16(beta), eps, _f16(C), M, K, _stream(stream)))
     return C
+
+
+def ffn_block(Y, W1, b1, W2, b2, gamma, beta, eps=1e-12, stream=None):
+    """ffn_block: LN(GELU(Y W1^T + b1) W2^T + b2 + Y) * gamma + beta in one fused kernel."""
+    out = torch.empty_like(Y)
+    _check(lib().bbh_ffn_block(_f16(Y), _f16(W1), _f16(b1), _f16(W2), _f16(b2), _f16(gamma), _f16(beta), eps,
+                               _f16(out), Y.shape[0], _stream(stream)))
+    return out
 
 
 def layernorm(x, gamma, beta, eps=1e-12, residual=None, stream=None):

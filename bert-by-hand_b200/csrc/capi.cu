@@ -289,6 +289,8 @@ struct bbh_ws {
   int32_t* meta = nullptr;
   int* err = nullptr;
   std::vector<GemmPlan> plans;  // 4 per layer: QKV, O+LN, FFN1+GELU, FFN2+LN
+  std::vector<bbh::MlpPlan> mlp_plans;  // per layer: the fused FFN block
+  bool fused_ffn = false;               // measured slower than the two GEMMs (see mlp_fused.cu)
   bool use_graph = true;
   cudaStream_t cap_stream = nullptr;
   cudaGraph_t graph = nullptr;
@@ -326,6 +328,7 @@ namespace {
 int build_plans(bbh_ws* ws, const bbh_weights* w) {
   using namespace bbh;
   ws->plans.assign(size_t(w->layers) * 4, GemmPlan{});
+  ws->mlp_plans.assign(size_t(w->layers), MlpPlan{});
   for (int l = 0; l < w->layers; ++l) {
     const LayerPtrs& L = w->L[l];
     GemmPlan* P = &ws->plans[size_t(l) * 4];
@@ -343,6 +346,15 @@ int build_plans(bbh_ws* ws, const bbh_weights* w) {
     P[2].p.C = ws->inter; P[2].p.ldc = kFfn; P[2].p.bias = L.i_b;
     P[3].p.C = ws->X;    P[3].p.ldc = kHidden; P[3].p.bias = L.o2_b;
     P[3].p.gamma = L.ln2_g; P[3].p.beta = L.ln2_b;
+    MlpPlan& M = ws->mlp_plans[size_t(l)];
+    rc = make_mlp_plan(&M, ws->Y, T, L.i_w, L.o2_w, ws->X, ws->num_sms);
+    if (rc) return fail(rc, "tensor map encoding failed (FFN block)");
+    M.p.b1 = L.i_b;
+    M.p.b2 = L.o2_b;
+    M.p.gamma = L.ln2_g;
+    M.p.beta = L.ln2_b;
+    M.p.rows_dev = ws->meta + 1;
+    M.p.err = ws->err;
     for (int j = 0; j < 4; ++j) {
       P[j].p.rows_dev = ws->meta + 1;
       P[j].p.err = ws->err;
@@ -421,9 +433,18 @@ int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh
         BBH_CUDA(launch_attention(ap, attention_grid(ws->num_sms), s));
       }
     }
-    for (int j = 1; j < 4; ++j) {
-      KernelMark km(ws, s, 2 + j);
-      BBH_CUDA(launch_gemm(P[j], s));
+    {
+      KernelMark km(ws, s, 3);
+      BBH_CUDA(launch_gemm(P[1], s));
+    }
+    if (ws->fused_ffn) {
+      KernelMark km(ws, s, 7);
+      BBH_CUDA(launch_mlp(ws->mlp_plans[size_t(l)], s));
+    } else {
+      for (int j = 2; j < 4; ++j) {
+        KernelMark km(ws, s, 2 + j);
+        BBH_CUDA(launch_gemm(P[j], s));
+      }
     }
     if (dump) BBH_CUDA(cudaMemcpyAsync(dump + plane * (l + 1), ws->X, plane * 2, cudaMemcpyDeviceToDevice, s));
   }
@@ -616,6 +637,15 @@ void bbh_ws_free(bbh_ws* ws) {
   delete ws;
 }
 
+int bbh_ws_set_ffn_fusion(bbh_ws* ws, int enable) {
+  if (!ws) return fail(BBH_ERR_ARG, "null workspace");
+  if ((enable != 0) != ws->fused_ffn) {
+    ws->fused_ffn = enable != 0;
+    drop_graph(ws);  // the captured graph holds the other launch sequence
+  }
+  return BBH_OK;
+}
+
 int bbh_ws_set_graph(bbh_ws* ws, int enable) {
   if (!ws) return fail(BBH_ERR_ARG, "null workspace");
   ws->use_graph = enable != 0;
@@ -656,7 +686,7 @@ int bbh_ws_kernel_times(bbh_ws* ws, double* ms, int64_t* counts) {
 
 int bbh_launches_per_forward(const bbh_ws* ws) {
   if (!ws || !ws->w) return 0;
-  const int per_layer = ws->max_len > bbh::kAttnTcMaxLen ? 6 : 5;
+  const int per_layer = (ws->max_len > bbh::kAttnTcMaxLen ? 6 : 5) - (ws->fused_ffn ? 1 : 0);
   return 2 + per_layer * ws->w->layers;
 }
 
@@ -787,6 +817,31 @@ int bbh_linear_residual_layernorm(const uint16_t* A, const uint16_t* W, const ui
                                   const uint16_t* residual, const uint16_t* gamma, const uint16_t* beta, float eps,
                                   uint16_t* C, int M, int K, void* stream) {
   return unit_gemm(A, W, bias, residual, gamma, beta, eps, C, M, bbh::kHidden, K, bbh::kEpiResLN, stream);
+}
+
+int bbh_ffn_block(const uint16_t* Y, const uint16_t* W1, const uint16_t* b1, const uint16_t* W2, const uint16_t* b2,
+                  const uint16_t* gamma, const uint16_t* beta, float eps, uint16_t* out, int M, void* stream) {
+  using namespace bbh;
+  if (!Y || !W1 || !b1 || !W2 || !b2 || !gamma || !beta || !out || M <= 0)
+    return fail(BBH_ERR_ARG, "bbh_ffn_block: bad arguments");
+  if ((reinterpret_cast<uintptr_t>(Y) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(BBH_ERR_ARG, "bbh_ffn_block: pointers must be 16-byte aligned");
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  MlpPlan plan;
+  rc = make_mlp_plan(&plan, reinterpret_cast<const __half*>(Y), M, reinterpret_cast<const __half*>(W1),
+                     reinterpret_cast<const __half*>(W2), reinterpret_cast<__half*>(out), g_num_sms(dev));
+  if (rc) return fail(rc, "bbh_ffn_block: tensor map encoding failed (alignment)");
+  plan.p.b1 = reinterpret_cast<const __half*>(b1);
+  plan.p.b2 = reinterpret_cast<const __half*>(b2);
+  plan.p.gamma = reinterpret_cast<const __half*>(gamma);
+  plan.p.beta = reinterpret_cast<const __half*>(beta);
+  plan.p.eps = eps;
+  plan.p.rows = M;
+  plan.p.err = unit_err_word(dev);
+  BBH_CUDA(launch_mlp(plan, static_cast<cudaStream_t>(stream)));
+  return BBH_OK;
 }
 
 int bbh_layernorm(const uint16_t* x, const uint16_t* gamma, const uint16_t* beta, uint16_t* y, int M, int D,

@@ -432,8 +432,8 @@ static PFN_encodeTiled get_encode_fn() {
 // Row-major [rows, cols] fp16 matrix with row stride ld elements; box = box_cols x box_rows
 // with the given swizzle (operands: 64 x rows, 128-byte swizzle, matching
 // sw128_kmajor_desc; outputs: 32 x 32, 64-byte swizzle, matching ChunkStore).
-static int encode_2d(CUtensorMap* map, const __half* base, int rows, int cols, int ld, int box_cols, int box_rows,
-                     CUtensorMapSwizzle swz) {
+int encode_2d(CUtensorMap* map, const __half* base, int rows, int cols, int ld, int box_cols, int box_rows,
+              CUtensorMapSwizzle swz) {
   PFN_encodeTiled enc = get_encode_fn();
   if (!enc) return BBH_ERR_CUDA;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16) return BBH_ERR_ARG;

@@ -60,9 +60,41 @@ struct GemmPlan {
 // stride ldc (written by TMA stores, clipped at rows_cap and N). Returns 0 or a BBH_ERR_*.
 int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const __half* W, int N, int K,
                    __half* C, int ldc, int epi, int num_sms);
+// Tensor map of a row-major [rows, cols] fp16 matrix (row stride ld elements), box
+// box_cols x box_rows with the given swizzle. Returns 0 or a BBH_ERR_*.
+int encode_2d(CUtensorMap* map, const __half* base, int rows, int cols, int ld, int box_cols, int box_rows,
+              CUtensorMapSwizzle swz);
 // kEpiResLN: the residual [rows_cap, N] with row stride ldr (read with TMA, 16-byte aligned).
 int set_gemm_residual(GemmPlan* plan, const __half* R, int ldr);
 cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream);
+
+// ------------------------------------------------------------------ fused FFN block
+// out = LayerNorm(GELU(Y W1^T + b1) W2^T + b2 + residual) * gamma + beta (mlp_fused.cu)
+struct MlpParams {
+  __half* C;               // [rows, ldc] output
+  int ldc;
+  const __half* residual;  // [rows, ldr]
+  int ldr;
+  const __half* b1;        // [1536]
+  const __half* b2;        // [384]
+  const __half* gamma;     // [384]
+  const __half* beta;      // [384]
+  float eps;
+  const int* rows_dev;     // when non-null the row count is read from device memory
+  int rows;
+  int* err;
+};
+struct MlpPlan {
+  CUtensorMap tmX;   // Y [rows_cap, 384]
+  CUtensorMap tmW1;  // [1536, 384]
+  CUtensorMap tmW2;  // [384, 1536]
+  MlpParams p;
+  int grid;
+};
+// Y: [rows_cap, 384] input (also the default residual); W1/W2 nn.Linear layouts; C output.
+int make_mlp_plan(MlpPlan* plan, const __half* Y, int rows_cap, const __half* W1, const __half* W2, __half* C,
+                  int num_sms);
+cudaError_t launch_mlp(const MlpPlan& plan, cudaStream_t stream);
 
 // ------------------------------------------------------------------ other kernels
 // Forward-call description consumed by the first kernel of a forward. It is passed by

@@ -81,6 +81,11 @@ BBH_API int bbh_weights_layers(const bbh_weights* w);
  * BBH_ERR_CAPACITY instead of overflowing. One workspace per concurrent stream. */
 BBH_API int bbh_ws_create(const bbh_weights* w, int max_tokens, int max_batch, int max_len, bbh_ws** out);
 BBH_API void bbh_ws_free(bbh_ws* ws);
+/* 1: the feed-forward block of every layer runs as one fused kernel (FFN1, GELU, FFN2,
+ * residual LayerNorm; the intermediate stays on chip); 0 (default): two GEMM launches
+ * through an HBM intermediate, as the reference's ffn_block -- currently the faster of the
+ * two on B200 (the fused kernel's 128-wide 1-SM tiles use the tensor cores less well). */
+BBH_API int bbh_ws_set_ffn_fusion(bbh_ws* ws, int enable);
 /* 1 (default): bbh_embed* replay one captured CUDA graph per workspace; 0: eager launches. */
 BBH_API int bbh_ws_set_graph(bbh_ws* ws, int enable);
 /* Synchronises the device, returns the workspace's device error code (0 = none) and
@@ -93,8 +98,8 @@ BBH_API int bbh_launches_per_forward(const bbh_ws* ws);
  * bbh_ws_kernel_times synchronises, adds the elapsed milliseconds and launch counts per
  * kernel kind into ms[BBH_KERNEL_KINDS] / counts[BBH_KERNEL_KINDS] and resets them.
  * Kinds: 0 embed+LN, 1 QKV GEMM, 2 attention, 3 O GEMM+LN, 4 FFN1 GEMM+GELU,
- * 5 FFN2 GEMM+LN, 6 pool+L2. */
-#define BBH_KERNEL_KINDS 7
+ * 5 FFN2 GEMM+LN, 6 pool+L2, 7 fused FFN block (4 and 5 only without fusion). */
+#define BBH_KERNEL_KINDS 8
 BBH_API int bbh_ws_set_kernel_timing(bbh_ws* ws, int enable);
 BBH_API int bbh_ws_kernel_times(bbh_ws* ws, double* ms, int64_t* counts);
 
@@ -132,6 +137,12 @@ BBH_API int bbh_linear(const uint16_t* A, const uint16_t* W, const uint16_t* bia
 BBH_API int bbh_linear_residual_layernorm(const uint16_t* A, const uint16_t* W, const uint16_t* bias,
                                   const uint16_t* residual, const uint16_t* gamma, const uint16_t* beta, float eps,
                                   uint16_t* C, int M, int K, void* stream);
+/* ffn_block (src/model/encoder.cu:52-64) as one kernel: out = LN(GELU(Y W1^T + b1) W2^T + b2
+ * + Y) * gamma + beta; Y/out [M, 384], W1 [1536, 384], W2 [384, 1536] (nn.Linear
+ * layouts); 16-byte aligned. */
+BBH_API int bbh_ffn_block(const uint16_t* Y, const uint16_t* W1, const uint16_t* b1, const uint16_t* W2,
+                          const uint16_t* b2, const uint16_t* gamma, const uint16_t* beta, float eps, uint16_t* out,
+                          int M, void* stream);
 /* launch_layernorm (src/kernels/layernorm.h): y = LN(x [+ residual]); D must be 384. */
 BBH_API int bbh_layernorm(const uint16_t* x, const uint16_t* gamma, const uint16_t* beta, uint16_t* y, int M, int D,
                   float eps, const uint16_t* residual, void* stream);

@@ -233,3 +233,24 @@ def test_device_flags_bad_tokens_and_seqlens(gw0):
     ok = ws.embed_varlen(i32(np.full(20, 1000)), None, i32([0, 4, 20]), 16)
     torch.cuda.synchronize()
     assert ws.device_error() == 0 and torch.isfinite(ok.float()).all()
+
+
+def test_fused_ffn_matches_two_gemm_path(gw0):
+    """The fused FFN block and the two-GEMM path give the same forward (within fp16 noise)."""
+    import bbh
+    import synthetic as sy
+
+    lengths = sy.lengths_uniform(200, 8, 128, 5)
+    c = sy.bucketed_corpus(lengths, 200, 5)
+    b = c.batches[0]
+    ws = bbh.Workspace(gw0, b.tokens, 200, 128)
+    d = lambda a: torch.as_tensor(np.asarray(a), dtype=torch.int32, device=DEV)
+    ids, types, cu = d(c.ids), d(c.types), d(b.cu)
+    plain = ws.embed_varlen(ids, types, cu, b.max_len).float().cpu().numpy()
+    n_plain = ws.launches_per_forward
+    ws.set_ffn_fusion(True)
+    fused = ws.embed_varlen(ids, types, cu, b.max_len).float().cpu().numpy()
+    assert ws.launches_per_forward == n_plain - 6
+    assert ws.device_error() == 0
+    assert cos_rows(fused, plain).min() >= 0.99995
+    assert np.abs(fused - plain).max() < 5e-3
