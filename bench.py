@@ -215,6 +215,8 @@ def main():
     ap.add_argument("--no-gather", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--lanes", type=int, default=2, choices=[1, 2],
+                    help="compute lanes: alternate batches over this many workspaces / streams")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -248,6 +250,8 @@ def main():
         max_tokens = batch * S
         max_len = S
     ws = bbh.Workspace(gw, max_tokens, batch, max_len)
+    lanes = [ws] + [bbh.Workspace(gw, max_tokens, batch, max_len) for _ in range(args.lanes - 1)]
+    ws.set_corpus_lanes(args.lanes)
 
     i32 = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.int32, device=dev)
     emb = torch.empty((n, 384), dtype=torch.float16, device=dev)
@@ -263,16 +267,25 @@ def main():
         pmask[:, :L] = 1
         d_ids, d_types, d_mask = i32(pid), i32(np.zeros_like(pid)), i32(pmask)
     stream = torch.cuda.current_stream(dev)
+    lane_streams = [stream] + [torch.cuda.Stream(dev) for _ in range(args.lanes - 1)]
 
-    def forward_all():
+    def forward_all(nlanes=None):
+        # batch bi runs on lane bi % nlanes (its own workspace and stream); the current
+        # stream orders the lanes' work before and after
+        nl = nlanes or len(lanes)
+        for ls in lane_streams[1:nl]:
+            ls.wait_stream(stream)
         for bi, b in enumerate(corpus.batches):
             out = emb[b.first:b.first + b.count]
+            lw, lst = lanes[bi % nl], lane_streams[bi % nl]
             if packed:
-                ws.embed_varlen(d_ids[b.tok_start:b.tok_start + b.tokens], d_types[b.tok_start:b.tok_start + b.tokens],
-                                d_cu[bi], b.max_len, out=out)
+                lw.embed_varlen(d_ids[b.tok_start:b.tok_start + b.tokens], d_types[b.tok_start:b.tok_start + b.tokens],
+                                d_cu[bi], b.max_len, out=out, stream=lst)
             else:
-                ws.embed(d_ids[b.first:b.first + b.count], d_types[b.first:b.first + b.count],
-                         d_mask[b.first:b.first + b.count], out=out)
+                lw.embed(d_ids[b.first:b.first + b.count], d_types[b.first:b.first + b.count],
+                         d_mask[b.first:b.first + b.count], out=out, stream=lst)
+        for ls in lane_streams[1:nl]:
+            stream.wait_stream(ls)
 
     gather = world > 1 and not args.no_gather
     gathered = torch.empty((world * n, 384), dtype=torch.float16, device=dev) if gather else None
@@ -379,7 +392,7 @@ def main():
     tok_per_step = int(sum(b.tokens for b in corpus.batches)) if packed else n * spec[2]
     kt_steps = 1
     for _ in range(kt_steps):
-        forward_all()
+        forward_all(nlanes=1)
     kt = ws.kernel_times()
     ws.set_kernel_timing(False)
     hbm, tf_burst, tf_sust, peak_src = measured_peaks()
@@ -438,6 +451,7 @@ def main():
                 "gather": "NCCL all_gather of fp16 embeddings each step" if gather else "none",
                 "l2": "inputs larger than L2 (each step streams ~1 GB of activations per GPU)",
                 "graph": "one CUDA graph per workspace, re-pointed per batch",
+                "lanes": f"{args.lanes} (batches alternate over {args.lanes} workspaces / streams)",
             },
             "roofline": roofline,
             "kernels": per_kernel,

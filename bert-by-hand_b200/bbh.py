@@ -62,6 +62,7 @@ _SIGS = {
     "bbh_mean_pool_l2": (_I, [_P, _P, _P, _I, _P, _P]),
     "bbh_plan_batches": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, ctypes.POINTER(_I)]),
     "bbh_embed_corpus": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _P, _P]),
+    "bbh_ws_set_corpus_lanes": (_I, [_P, _I]),
     "bbh_vocab_load": (_I, [ctypes.c_char_p, _I, ctypes.POINTER(_P)]),
     "bbh_vocab_free": (None, [_P]),
     "bbh_vocab_size": (_I, [_P]),
@@ -196,6 +197,10 @@ class Workspace:
 
     def set_graph(self, enable: bool):
         _check(lib().bbh_ws_set_graph(self.handle, 1 if enable else 0))
+
+    def set_corpus_lanes(self, lanes: int):
+        """1 or 2 compute lanes for embed_corpus (2: alternate batches on a second workspace)."""
+        _check(lib().bbh_ws_set_corpus_lanes(self.handle, lanes))
 
     def set_ffn_fusion(self, enable: bool):
         _check(lib().bbh_ws_set_ffn_fusion(self.handle, 1 if enable else 0))

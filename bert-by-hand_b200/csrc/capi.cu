@@ -307,6 +307,7 @@ struct bbh_ws {
   // host corpus driver staging (csrc/corpus.cu), created on first use
   void* corpus_stage = nullptr;
   void (*corpus_stage_free)(void*) = nullptr;
+  int corpus_lanes = 1;
 };
 
 namespace bbh {
@@ -321,6 +322,7 @@ void** ws_corpus_stage(bbh_ws* ws, void (*free_fn)(void*)) {
   ws->corpus_stage_free = free_fn;
   return &ws->corpus_stage;
 }
+int ws_corpus_lanes(const bbh_ws* ws) { return ws->corpus_lanes; }
 }  // namespace bbh
 
 namespace {
@@ -635,6 +637,12 @@ void bbh_ws_free(bbh_ws* ws) {
   cudaFree(ws->arena);
   cudaSetDevice(prev);
   delete ws;
+}
+
+int bbh_ws_set_corpus_lanes(bbh_ws* ws, int lanes) {
+  if (!ws || lanes < 1 || lanes > 2) return fail(BBH_ERR_ARG, "bbh_ws_set_corpus_lanes: lanes must be 1 or 2");
+  ws->corpus_lanes = lanes;
+  return BBH_OK;
 }
 
 int bbh_ws_set_ffn_fusion(bbh_ws* ws, int enable) {

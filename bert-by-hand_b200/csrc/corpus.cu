@@ -6,7 +6,8 @@
 // workspace's token capacity as well as its sentence count, assigned to ranks by
 // longest-processing-time on their FLOPs, and run with two staging slots so the host
 // gather, the host->device copy, the forward and the device->host copy of neighbouring
-// batches overlap.
+// batches overlap. With two lanes (bbh_ws_set_corpus_lanes) alternate batches also run on a
+// second workspace and compute stream, so neighbouring forwards overlap on the GPU.
 #include "internal.h"
 #include "../../include/bbh.h"
 
@@ -39,6 +40,12 @@ struct Stage {
   int max_tokens = 0, max_batch = 0;
   cudaStream_t up = nullptr, down = nullptr;  // host->device, device->host copy streams
   Slot slot[2];
+  // second lane: a workspace of the same capacity and its own compute stream, so that the
+  // forwards of neighbouring batches can overlap (one batch's kernel tails and launch
+  // gaps are filled with the other's work)
+  int lanes = 1;
+  bbh_ws* ws2 = nullptr;
+  cudaStream_t s2 = nullptr;
 };
 
 void free_stage(void* p) {
@@ -61,6 +68,9 @@ void free_stage(void* p) {
     for (cudaEvent_t e : {s.h2d, s.fwd, s.d2h})
       if (e) cudaEventDestroy(e);
   }
+  if (st->s2) cudaStreamSynchronize(st->s2);
+  if (st->ws2) bbh_ws_free(st->ws2);
+  if (st->s2) cudaStreamDestroy(st->s2);
   if (st->up) cudaStreamDestroy(st->up);
   if (st->down) cudaStreamDestroy(st->down);
   cudaSetDevice(prev);
@@ -201,6 +211,16 @@ int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const
   }
   Stage& st = *static_cast<Stage*>(*slotp);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int lanes = bbh::ws_corpus_lanes(ws);
+  if (lanes == 2 && !st.ws2) {
+    int rc = bbh_ws_create(w, max_tokens, max_batch, max_len, &st.ws2);
+    if (!rc && cudaStreamCreateWithFlags(&st.s2, cudaStreamNonBlocking) != cudaSuccess)
+      rc = bbh::internal_fail(BBH_ERR_CUDA, "bbh_embed_corpus: stream creation failed");
+    if (rc) {
+      cudaSetDevice(prev);
+      return rc;
+    }
+  }
 
   // Copies a finished slot's embeddings to their corpus rows.
   auto drain = [&](Slot& sl) -> int {
@@ -220,6 +240,9 @@ int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const
   for (int b = 0; b < n_batches && rc == BBH_OK; ++b) {
     if (batch_rank[b] != rank) continue;
     Slot& sl = st.slot[k & 1];
+    // lane of this batch: its workspace and compute stream
+    bbh_ws* lws = (lanes == 2 && (k & 1)) ? st.ws2 : ws;
+    cudaStream_t ls = (lanes == 2 && (k & 1)) ? st.s2 : s;
     ++k;
     rc = drain(sl);  // also guarantees the slot's buffers are no longer in use
     if (rc) break;
@@ -242,15 +265,15 @@ int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const
               (!types || cudaMemcpyAsync(sl.d_types, sl.h_types, tb, cudaMemcpyHostToDevice, st.up) == cudaSuccess) &&
               cudaMemcpyAsync(sl.d_cu, sl.h_cu, size_t(count + 1) * sizeof(int32_t), cudaMemcpyHostToDevice, st.up) ==
                   cudaSuccess &&
-              cudaEventRecord(sl.h2d, st.up) == cudaSuccess && cudaStreamWaitEvent(s, sl.h2d, 0) == cudaSuccess;
+              cudaEventRecord(sl.h2d, st.up) == cudaSuccess && cudaStreamWaitEvent(ls, sl.h2d, 0) == cudaSuccess;
     if (!ok) {
       rc = bbh::internal_fail(BBH_ERR_CUDA, "bbh_embed_corpus: host->device copy failed");
       break;
     }
-    rc = bbh_embed_varlen(ws, w, sl.d_ids, types ? sl.d_types : nullptr, sl.d_cu, count, tok, std::max(blen, 1),
-                          sl.d_emb, s);
+    rc = bbh_embed_varlen(lws, w, sl.d_ids, types ? sl.d_types : nullptr, sl.d_cu, count, tok, std::max(blen, 1),
+                          sl.d_emb, ls);
     if (rc) break;
-    ok = cudaEventRecord(sl.fwd, s) == cudaSuccess && cudaStreamWaitEvent(st.down, sl.fwd, 0) == cudaSuccess &&
+    ok = cudaEventRecord(sl.fwd, ls) == cudaSuccess && cudaStreamWaitEvent(st.down, sl.fwd, 0) == cudaSuccess &&
          cudaMemcpyAsync(sl.h_emb, sl.d_emb, size_t(count) * BBH_HIDDEN * sizeof(uint16_t), cudaMemcpyDeviceToHost,
                          st.down) == cudaSuccess &&
          cudaEventRecord(sl.d2h, st.down) == cudaSuccess;
@@ -266,7 +289,8 @@ int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const
     sl.batch = -1;
   }
   if (!rc) {
-    const int dev_err = bbh_device_error(ws, 0);
+    int dev_err = bbh_device_error(ws, 0);
+    if (dev_err == 0 && st.ws2) dev_err = bbh_device_error(st.ws2, 0);
     if (dev_err < 0)
       rc = dev_err;
     else if (dev_err > 0)

@@ -19,6 +19,8 @@ void ws_limits(const bbh_ws* ws, int* device, int* max_tokens, int* max_batch, i
 // The workspace's slot for the corpus driver's staging state; free_fn releases it when
 // the workspace is freed.
 void** ws_corpus_stage(bbh_ws* ws, void (*free_fn)(void*));
+// Number of compute lanes the corpus driver uses for this workspace (1 or 2).
+int ws_corpus_lanes(const bbh_ws* ws);
 
 // ------------------------------------------------------------------ GEMM (tcgen05)
 enum Epilogue : int {

@@ -179,6 +179,11 @@ BBH_API int bbh_plan_batches(const int32_t* lengths, int n, int max_batch, int m
  * second copy stream, so the staging of one batch overlaps the forward of the previous
  * one. Returns when every result is in emb. Batches must fit the workspace (checked on the
  * host before anything runs); device-detected input errors return BBH_ERR_DEVICE. */
+/* Compute lanes of bbh_embed_corpus for this workspace: 1 (default) or 2. With 2 the driver
+ * creates (on first use, freed with ws) a second workspace of the same capacity and a
+ * second compute stream, and alternates batches between them so that neighbouring
+ * forwards overlap on the GPU (short-sentence corpora gain the most). */
+BBH_API int bbh_ws_set_corpus_lanes(bbh_ws* ws, int lanes);
 BBH_API int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
                              const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
                              const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb, void* stream);

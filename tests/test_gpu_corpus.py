@@ -94,3 +94,18 @@ def test_capacity_checked_before_work(setup):
         short.embed_corpus(ids, types, offsets, bbh.plan_batches(lengths, 96, 4096, 1))
     assert e.value.code == -2
     assert ws.device_error() == 0
+
+
+def test_two_lanes_bit_identical(setup):
+    """Two compute lanes (a second workspace and stream, alternate batches) give exactly the
+    one-lane results."""
+    bbh, w, gw, lengths, ids, types, offsets = setup
+    plan = bbh.plan_batches(lengths, 64, 4096, 1)
+    one = bbh.Workspace(gw, 4096, 64, 128).embed_corpus(ids, types, offsets, plan)
+    ws = bbh.Workspace(gw, 4096, 64, 128)
+    ws.set_corpus_lanes(2)
+    two = ws.embed_corpus(ids, types, offsets, plan)
+    assert plan.n_batches > 4
+    assert np.array_equal(one.view(np.uint16), two.view(np.uint16))
+    with pytest.raises(bbh.BBHError):
+        ws.set_corpus_lanes(3)
