@@ -363,6 +363,292 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(AttnParams 
   }
 }
 
+// ======================================================================== long sentences
+// Sentences of 129-512 tokens (the reference caps seq at 128; configs[4] runs 512): one CTA
+// item is (sentence, head, block of 128 query rows). Q of the block and all of the head's
+// K and V go to shared memory once (cp.async, 64-byte swizzle, zero-filled past the end);
+// the keys are then walked in blocks of 64 with the online softmax of flash attention:
+//   S_j = Q K_j^T (tcgen05, M = 128, N = 64) into one of two TMEM buffers, so the S-MMA of
+//   block j + 2 is queued behind the P.V-MMA of block j and overlaps the softmax of j + 1;
+//   thread t (query row t) keeps a reference max m and the sum l, and writes
+//   P_j = 2^(s*scale - m*scale) as fp16 pairs over the S columns it read. The reference is
+//   raised (and l and the row of O in TMEM rescaled) only when a block's max exceeds it by
+//   more than 2^8, so P stays <= 256 and most blocks need no rescale: then the P.V-MMA of
+//   block j is issued without waiting for the one of block j - 1. When some row does need
+//   it, the CTA waits once for the issued MMAs and rescales;
+//   O += P_j V_j (tcgen05, A = P from TMEM, V MN-major in shared memory).
+// Two threads per query row: warps w and w + 4 share TMEM lane quadrant w and take the
+// first and second 32 keys of each block (partial maxima and sums meet in shared memory).
+// TMEM: S buffers at columns [0, 64) and [64, 128), O at [128, 160) (256 allocated);
+// ~80 KB of shared memory: two CTAs (16 warps) per SM.
+constexpr int kLongThreads = 256;
+constexpr int kLongMax = 512;  // keys per sentence
+constexpr int kKeyBlk = 64;
+
+struct LongSmem {
+  uint8_t q[kTcRows * 64];
+  uint8_t k[kLongMax * 64];
+  uint8_t v[kLongMax * 64];
+  uint8_t keyok[kLongMax];
+  float part[2][kTcRows];  // per-half partial row max, then partial row sum
+  uint64_t bar_s[2], bar_o, bar_fix;
+  uint32_t tmem;
+  int abort_flag;
+  int cu[1];  // cached cu_seqlens follow
+};
+
+struct LongItem {
+  int item, h, qb, start, len;
+};
+
+// items are (head, sentence, query block), head-major like the short kernel
+__device__ __forceinline__ LongItem long_find(const int* cu, int batch, int item, int step, int items, int min_len) {
+  LongItem u;
+  for (; item < items; item += step) {
+    const int qb = item & 3;
+    const int rest = item >> 2;
+    const int b = rest % batch;
+    const int h = rest / batch;
+    const int start = cu[b];
+    const int len = cu[b + 1] - start;
+    if (len < min_len || len > kLongMax || qb * kTcRows >= len) continue;
+    u.item = item;
+    u.h = h;
+    u.qb = qb;
+    u.start = start;
+    u.len = len;
+    return u;
+  }
+  u.item = -1;
+  return u;
+}
+
+__global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnParams p) {
+  extern __shared__ uint8_t lg_raw[];
+  LongSmem& sm = *reinterpret_cast<LongSmem*>((reinterpret_cast<uintptr_t>(lg_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int batch = p.meta ? p.meta[0] : p.batch;
+  const uint8_t* tokmask = (p.meta && p.meta[3] == 0) ? nullptr : p.tokmask;
+  const int items = batch * kHeads * 4;
+  const int* cu = p.cu;
+  if (batch < kTcCuCache) {
+    for (int i = tid; i <= batch; i += kLongThreads) sm.cu[i] = p.cu[i];
+    cu = sm.cu;
+  }
+  if (tid == 0) {
+    mbar_init(&sm.bar_s[0], 1);
+    mbar_init(&sm.bar_s[1], 1);
+    mbar_init(&sm.bar_o, 1);
+    mbar_init(&sm.bar_fix, 1);
+    sm.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&sm.tmem, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem;
+  const uint32_t t_o = tmem + 128;
+  const int quad = warp & 3, half = warp >> 2;  // TMEM lane quadrant; key half of a block
+  const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+  volatile int* abort_flag = &sm.abort_flag;
+  constexpr uint32_t idesc_s = idesc_f16_f32(128, kKeyBlk);            // Q K^T, both K-major
+  constexpr uint32_t idesc_o = idesc_f16_f32(128, 32) | (1u << 16);    // P V, V MN-major
+  const float scale = p.scale_log2;
+  uint32_t ph_s[2] = {0, 0}, ph_o = 0, ph_fix = 0;
+  constexpr float kRescaleLog2 = 8.f;  // raise the reference max when a block exceeds it by 2^8
+
+  for (LongItem u = long_find(cu, batch, blockIdx.x, gridDim.x, items, p.min_len); u.item >= 0;
+       u = long_find(cu, batch, u.item + gridDim.x, gridDim.x, items, p.min_len)) {
+    const int len = u.len;
+    const int nkb = (len + kKeyBlk - 1) / kKeyBlk;
+    const int q0 = u.qb * kTcRows;
+    // ---- stage Q (128 rows), K and V (nkb * 64 rows) of this head
+    {
+      const __half* base = p.qkv + static_cast<size_t>(u.start) * kQkvLd + u.h * kHeadDim;
+      const uint32_t sq = smem_u32(sm.q), sk = smem_u32(sm.k), sv = smem_u32(sm.v);
+      const int c = tid & 3;
+      for (int r = tid >> 2; r < kTcRows; r += kLongThreads / 4) {
+        const bool ok = q0 + r < len;
+        const uint32_t off = r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
+        cp_async16_tc(sq + off, base + static_cast<size_t>(ok ? q0 + r : 0) * kQkvLd + c * 8, ok ? 16 : 0);
+      }
+      for (int r = tid >> 2; r < nkb * kKeyBlk; r += kLongThreads / 4) {
+        const bool ok = r < len;
+        const uint32_t off = r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
+        const __half* src = base + static_cast<size_t>(ok ? r : 0) * kQkvLd + c * 8;
+        cp_async16_tc(sk + off, src + kHidden, ok ? 16 : 0);
+        cp_async16_tc(sv + off, src + 2 * kHidden, ok ? 16 : 0);
+      }
+      if (tokmask)
+        for (int r = tid; r < nkb * kKeyBlk; r += kLongThreads) sm.keyok[r] = r < len ? tokmask[u.start + r] : 0;
+      cp_async_commit_tc();
+      cp_async_wait_tc<0>();
+      fence_async_shared();
+      __syncthreads();
+    }
+    auto issue_s = [&](int j) {
+      const int b = j & 1;
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk)
+        tc_mma_f16(tmem + b * kKeyBlk, sw64_kmajor_desc(smem_u32(sm.q) + kk * 32),
+                   sw64_kmajor_desc(smem_u32(sm.k) + j * kKeyBlk * 64 + kk * 32), idesc_s, kk);
+      tc_commit(&sm.bar_s[b]);
+    };
+    if (tid == 0) {
+      tc_fence_after();
+      issue_s(0);
+      if (nkb > 1) issue_s(1);
+    }
+    const int row = quad * 32 + (tid & 31);
+    const bool row_ok = q0 + row < len;
+    float m = -INFINITY, l = 0.f;
+    bool failed = false;
+    for (int j = 0; j < nkb; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&sm.bar_s[b], ph_s[b], abort_flag, nullptr)) {
+        failed = true;
+        break;
+      }
+      ph_s[b] ^= 1;
+      tc_fence_after();
+      float t[32];
+      tmem_ld32(tmem + lane_off + b * kKeyBlk + half * 32, t);
+      // usable keys of this half block: k < len (and the token mask), for a valid query row
+      const int k0 = j * kKeyBlk + half * 32;
+      uint32_t mk;
+      {
+        const int n_ok = min(max(len - k0, 0), 32);
+        uint32_t mm = n_ok >= 32 ? 0xffffffffu : ((1u << n_ok) - 1u);
+        if (tokmask) {
+          uint32_t km = 0;
+          for (int e = 0; e < 32; ++e) km |= (sm.keyok[k0 + e] ? 1u : 0u) << e;
+          mm &= km;
+        }
+        mk = row_ok ? mm : 0u;
+      }
+      float pmax = -INFINITY;
+      if (mk == 0xffffffffu) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pmax = fmaxf(pmax, t[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pmax = fmaxf(pmax, (mk >> e) & 1u ? t[e] : -INFINITY);
+      }
+      sm.part[half][row] = pmax;
+      __syncthreads();
+      const float bmax = fmaxf(pmax, sm.part[half ^ 1][row]);
+      // raise the reference max if this block exceeds it by more than 2^8 (always for the
+      // first usable block); alpha rescales what was accumulated against the old reference
+      float alpha = 1.f;
+      const bool raise = bmax != -INFINITY && (m == -INFINITY || (bmax - m) * scale > kRescaleLog2);
+      if (raise) {
+        alpha = m == -INFINITY ? 0.f : exp2f((m - bmax) * scale);
+        l *= alpha;
+        m = bmax;
+      }
+      // O holds earlier blocks' P.V (j > 0): rescale its rows once the issued MMAs have landed
+      if (__syncthreads_or(raise && j > 0 && alpha != 1.f)) {
+        if (tid == 0) tc_commit(&sm.bar_fix);  // arrives when every MMA issued so far is done
+        if (!mbar_wait(&sm.bar_fix, ph_fix, abort_flag, nullptr)) {
+          failed = true;
+          break;
+        }
+        ph_fix ^= 1;
+        tc_fence_after();
+        if (half == 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          float o[32];
+          tmem_ld32(t_o + lane_off, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] *= alpha;
+          tmem_st32(t_o + lane_off, o);
+        }
+      }
+      const float msc = m == -INFINITY ? 0.f : m * scale;
+      float bsum = 0.f;
+      {
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float e0, e1;
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(fmaf(t[e], scale, -msc)));
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(fmaf(t[e + 1], scale, -msc)));
+          e0 = (mk >> e) & 1u ? e0 : 0.f;
+          e1 = (mk >> (e + 1)) & 1u ? e1 : 0.f;
+          bsum += e0 + e1;
+          w[e >> 1] = pack_half2(e0, e1);
+        }
+        tmem_st16(tmem + lane_off + b * kKeyBlk + half * 16, w);  // P pairs over the S columns
+      }
+      l += bsum;  // this half's share of the row sum (both halves use the same reference m)
+      tmem_wait_st();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kKeyBlk / 16; ++k)
+          tc_mma_f16_ts(t_o, tmem + b * kKeyBlk + k * 8,
+                        sw64_mnmajor_desc(smem_u32(sm.v) + (j * (kKeyBlk / 16) + k) * 1024), idesc_o,
+                        (j > 0 || k > 0) ? 1u : 0u);
+        if (j + 1 == nkb) tc_commit(&sm.bar_o);  // the item's last P.V
+        if (j + 2 < nkb) issue_s(j + 2);        // queued behind this P.V, which reads the buffer
+      }
+    }
+    if (failed) break;
+    sm.part[half][row] = l;
+    __syncthreads();
+    const float l_row = l + sm.part[half ^ 1][row];
+    if (!mbar_wait(&sm.bar_o, ph_o, abort_flag, nullptr)) break;
+    ph_o ^= 1;
+    tc_fence_after();
+    {
+      float o[32];
+      tmem_ld32(t_o + lane_off, o);
+      if (row_ok) {
+        const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
+        __half* out = p.ctx + static_cast<size_t>(u.start + q0 + row) * kHidden + u.h * kHeadDim + half * 16;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          uint4 wv;
+          uint32_t* ww = reinterpret_cast<uint32_t*>(&wv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            ww[e] = pack_half2(o[half * 16 + j * 8 + 2 * e] * inv, o[half * 16 + j * 8 + 2 * e + 1] * inv);
+          *reinterpret_cast<uint4*>(out + j * 8) = wv;
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // shared memory and TMEM free for the next item
+  }
+  cp_async_wait_tc<0>();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+int attention_long_smem() { return static_cast<int>(sizeof(LongSmem)) + 4 * kTcCuCache + 1024; }
+
+cudaError_t launch_attention_long(const AttnParams& p, int grid, cudaStream_t stream) {
+  const int smem = attention_long_smem();
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attention_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  attention_long_kernel<<<grid, kLongThreads, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
 int attention_tc_smem() { return static_cast<int>(sizeof(TcSmem)) + 4 * kTcCuCache + 1024; }
 
 cudaError_t launch_attention_tc(const AttnParams& p, int grid, cudaStream_t stream) {

@@ -432,7 +432,7 @@ int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh
       BBH_CUDA(launch_attention_tc(ap, 4 * ws->num_sms, s));
       if (ws->max_len > kAttnTcMaxLen) {
         ap.min_len = kAttnTcMaxLen + 1;
-        BBH_CUDA(launch_attention(ap, attention_grid(ws->num_sms), s));
+        BBH_CUDA(launch_attention_long(ap, 2 * ws->num_sms, s));
       }
     }
     {
@@ -884,7 +884,7 @@ int bbh_attention_varlen(const uint16_t* qkv, uint16_t* ctx, const int32_t* cu_s
   BBH_CUDA(bbh::launch_attention_tc(ap, 4 * g_num_sms(dev), static_cast<cudaStream_t>(stream)));
   if (max_len > bbh::kAttnTcMaxLen) {
     ap.min_len = bbh::kAttnTcMaxLen + 1;
-    BBH_CUDA(bbh::launch_attention(ap, bbh::attention_grid(g_num_sms(dev)), static_cast<cudaStream_t>(stream)));
+    BBH_CUDA(bbh::launch_attention_long(ap, 2 * g_num_sms(dev), static_cast<cudaStream_t>(stream)));
   }
   return BBH_OK;
 }

@@ -134,12 +134,11 @@ struct AttnParams {
   const int32_t* meta;     // {B, T, max_len, has_mask}, or null to use the host values below
   int batch;
   int max_len;
-  int min_len;             // sentences shorter than this are skipped (the tcgen05 kernel has them)
+  int min_len;             // sentences shorter than this are skipped (the short-sentence kernel has them)
   float scale_log2;        // log2(e) / sqrt(head_dim)
 };
-// mma.sync kernel: any length (used for sentences longer than kAttnTcMaxLen)
-cudaError_t launch_attention(const AttnParams& p, int grid, cudaStream_t stream);
-int attention_grid(int num_sms);
+// tcgen05 flash-style kernel for sentences of kAttnTcMaxLen+1 .. 512 tokens (min_len)
+cudaError_t launch_attention_long(const AttnParams& p, int grid, cudaStream_t stream);
 // tcgen05 kernel: sentences of at most kAttnTcMaxLen tokens
 constexpr int kAttnTcMaxLen = 128;
 cudaError_t launch_attention_tc(const AttnParams& p, int grid, cudaStream_t stream);
