@@ -87,37 +87,62 @@ __global__ void __launch_bounds__(kRowThreads) embed_ln_kernel(EmbedParams p) {
     }
   }
 
-  for (int t = gwarp; t < p.total; t += warps) {
-    int pos;
-    if (packed) {
-      // last segment whose start <= t (cu_seqlens is non-decreasing)
-      int lo = 0, hi = p.batch;  // invariant: cu[lo] <= t < cu[hi]
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (__ldg(p.cu_seqlens + mid) <= t) lo = mid; else hi = mid;
+  // Each warp takes `chunk` consecutive tokens at a time (2..8, enough to spread the
+  // forward's tokens over all warps): lane l < chunk resolves token base + l (its segment
+  // by binary search, position, ids, mask, validation) in parallel, then the warp gathers
+  // and normalises the rows two at a time so both tokens' loads are in flight.
+  const int chunk = min(8, max(2, ((p.total + warps - 1) / warps + 1) & ~1));
+  for (int base = gwarp * chunk; base < p.total; base += warps * chunk) {
+    const int t = base + lane;
+    const bool valid = lane < chunk && t < p.total;
+    int pos = 0, id = 0, ty = 0;
+    if (valid) {
+      if (packed) {
+        // last segment whose start <= t (cu_seqlens is non-decreasing)
+        int lo = 0, hi = p.batch;  // invariant: cu[lo] <= t < cu[hi]
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (__ldg(p.cu_seqlens + mid) <= t) lo = mid; else hi = mid;
+        }
+        pos = t - __ldg(p.cu_seqlens + lo);
+      } else {
+        pos = t % p.seq;
       }
-      pos = t - __ldg(p.cu_seqlens + lo);
-    } else {
-      pos = t % p.seq;
-    }
-    int id = __ldg(p.ids + t);
-    int ty = p.types ? __ldg(p.types + t) : 0;
-    if (lane == 0) {
+      id = __ldg(p.ids + t);
+      ty = p.types ? __ldg(p.types + t) : 0;
       if (id < 0 || id >= kVocab || ty < 0 || ty >= kTypes) set_dev_error(p.err, kDevBadToken);
       if (pos >= kMaxPos) set_dev_error(p.err, kDevBadPosition);
       p.ws_tokmask[t] = p.mask ? static_cast<uint8_t>(__ldg(p.mask + t) != 0) : uint8_t(1);
+      id = (id < 0 || id >= kVocab) ? 0 : id;
+      ty = (ty < 0 || ty >= kTypes) ? 0 : ty;
+      pos = pos >= kMaxPos ? kMaxPos - 1 : pos;
     }
-    id = (id < 0 || id >= kVocab) ? 0 : id;
-    ty = (ty < 0 || ty >= kTypes) ? 0 : ty;
-    pos = pos >= kMaxPos ? kMaxPos - 1 : pos;
-    float f[12], a[12], c[12];
-    load_row12(p.word + static_cast<size_t>(id) * kHidden, lane, f);
-    load_row12(p.pos + static_cast<size_t>(pos) * kHidden, lane, a);
-    load_row12(p.type + static_cast<size_t>(ty) * kHidden, lane, c);
+    const int n = min(chunk, p.total - base);
+    for (int k = 0; k < n; k += 2) {
+      const bool two = k + 1 < n;
+      const int id0 = __shfl_sync(0xffffffffu, id, k), pos0 = __shfl_sync(0xffffffffu, pos, k);
+      const int ty0 = __shfl_sync(0xffffffffu, ty, k);
+      const int id1 = __shfl_sync(0xffffffffu, id, k + 1);
+      const int pos1 = __shfl_sync(0xffffffffu, pos, k + 1);
+      const int ty1 = __shfl_sync(0xffffffffu, ty, k + 1);
+      float f0[12], f1[12], a[12], c[12];
+      load_row12(p.word + static_cast<size_t>(id0) * kHidden, lane, f0);
+      if (two) load_row12(p.word + static_cast<size_t>(id1) * kHidden, lane, f1);
+      load_row12(p.pos + static_cast<size_t>(pos0) * kHidden, lane, a);
+      load_row12(p.type + static_cast<size_t>(ty0) * kHidden, lane, c);
 #pragma unroll
-    for (int i = 0; i < 12; ++i) f[i] += a[i] + c[i];
-    warp_layernorm12(f, p.gamma, p.beta, lane, p.eps);
-    store_row12(p.out + static_cast<size_t>(t) * kHidden, lane, f);
+      for (int i = 0; i < 12; ++i) f0[i] += a[i] + c[i];
+      warp_layernorm12(f0, p.gamma, p.beta, lane, p.eps);
+      store_row12(p.out + static_cast<size_t>(base + k) * kHidden, lane, f0);
+      if (two) {
+        load_row12(p.pos + static_cast<size_t>(pos1) * kHidden, lane, a);
+        load_row12(p.type + static_cast<size_t>(ty1) * kHidden, lane, c);
+#pragma unroll
+        for (int i = 0; i < 12; ++i) f1[i] += a[i] + c[i];
+        warp_layernorm12(f1, p.gamma, p.beta, lane, p.eps);
+        store_row12(p.out + static_cast<size_t>(base + k + 1) * kHidden, lane, f1);
+      }
+    }
   }
 }
 
