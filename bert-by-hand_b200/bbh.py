@@ -46,6 +46,7 @@ _SIGS = {
     "bbh_ws_free": (None, [_P]),
     "bbh_ws_set_graph": (_I, [_P, _I]),
     "bbh_ws_set_ffn_fusion": (_I, [_P, _I]),
+    "bbh_ws_set_pdl": (_I, [_P, _I]),
     "bbh_device_error": (_I, [_P, _I]),
     "bbh_launches_per_forward": (_I, [_P]),
     "bbh_ws_set_kernel_timing": (_I, [_P, _I]),
@@ -201,6 +202,9 @@ class Workspace:
     def set_corpus_lanes(self, lanes: int):
         """1 or 2 compute lanes for embed_corpus (2: alternate batches on a second workspace)."""
         _check(lib().bbh_ws_set_corpus_lanes(self.handle, lanes))
+
+    def set_pdl(self, enable: bool):
+        _check(lib().bbh_ws_set_pdl(self.handle, 1 if enable else 0))
 
     def set_ffn_fusion(self, enable: bool):
         _check(lib().bbh_ws_set_ffn_fusion(self.handle, 1 if enable else 0))

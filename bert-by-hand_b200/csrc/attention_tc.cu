@@ -167,6 +167,8 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(AttnParams 
   extern __shared__ uint8_t tc_raw[];
   TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();  // Q/K/V and the sentence table come from the previous kernels
   const int warp = tid >> 5;
 
   const int batch = p.meta ? p.meta[0] : p.batch;
@@ -427,6 +429,8 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
   extern __shared__ uint8_t lg_raw[];
   LongSmem& sm = *reinterpret_cast<LongSmem*>((reinterpret_cast<uintptr_t>(lg_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
   const int warp = tid >> 5;
   const int batch = p.meta ? p.meta[0] : p.batch;
   const uint8_t* tokmask = (p.meta && p.meta[3] == 0) ? nullptr : p.tokmask;
@@ -635,7 +639,7 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
 
 int attention_long_smem() { return static_cast<int>(sizeof(LongSmem)) + 4 * kTcCuCache + 1024; }
 
-cudaError_t launch_attention_long(const AttnParams& p, int grid, cudaStream_t stream) {
+cudaError_t launch_attention_long(const AttnParams& p, int grid, cudaStream_t stream, bool pdl) {
   const int smem = attention_long_smem();
   static bool attr_set[64] = {};
   int dev = 0;
@@ -645,13 +649,12 @@ cudaError_t launch_attention_long(const AttnParams& p, int grid, cudaStream_t st
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  attention_long_kernel<<<grid, kLongThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  return launch_ex(attention_long_kernel, dim3(grid), dim3(kLongThreads), smem, stream, pdl, 1, p);
 }
 
 int attention_tc_smem() { return static_cast<int>(sizeof(TcSmem)) + 4 * kTcCuCache + 1024; }
 
-cudaError_t launch_attention_tc(const AttnParams& p, int grid, cudaStream_t stream) {
+cudaError_t launch_attention_tc(const AttnParams& p, int grid, cudaStream_t stream, bool pdl) {
   const int smem = attention_tc_smem();
   static bool attr_set[64] = {};
   int dev = 0;
@@ -661,8 +664,7 @@ cudaError_t launch_attention_tc(const AttnParams& p, int grid, cudaStream_t stre
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  attention_tc_kernel<<<grid, kTcThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  return launch_ex(attention_tc_kernel, dim3(grid), dim3(kTcThreads), smem, stream, pdl, 1, p);
 }
 
 }  // namespace bbh

@@ -291,6 +291,7 @@ struct bbh_ws {
   std::vector<GemmPlan> plans;  // 4 per layer: QKV, O+LN, FFN1+GELU, FFN2+LN
   std::vector<bbh::MlpPlan> mlp_plans;  // per layer: the fused FFN block
   bool fused_ffn = false;               // measured slower than the two GEMMs (see mlp_fused.cu)
+  bool pdl = true;                      // programmatic dependent launch between the forward's kernels
   bool use_graph = true;
   cudaStream_t cap_stream = nullptr;
   cudaGraph_t graph = nullptr;
@@ -409,7 +410,7 @@ int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh
   const int row_grid = ws->num_sms * 8;
   {
     KernelMark km(ws, s, 0);
-    BBH_CUDA(launch_embed_ln(ep, row_grid, s));
+    BBH_CUDA(launch_embed_ln(ep, row_grid, s, ws->pdl));
   }
   const size_t plane = size_t(total) * kHidden;
   if (dump) BBH_CUDA(cudaMemcpyAsync(dump, ws->X, plane * 2, cudaMemcpyDeviceToDevice, s));
@@ -424,28 +425,28 @@ int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh
     const GemmPlan* P = &ws->plans[size_t(l) * 4];
     {
       KernelMark km(ws, s, 1);
-      BBH_CUDA(launch_gemm(P[0], s));
+      BBH_CUDA(launch_gemm(P[0], s, ws->pdl));
     }
     {
       KernelMark km(ws, s, 2);
       ap.min_len = 0;
-      BBH_CUDA(launch_attention_tc(ap, 4 * ws->num_sms, s));
+      BBH_CUDA(launch_attention_tc(ap, 4 * ws->num_sms, s, ws->pdl));
       if (ws->max_len > kAttnTcMaxLen) {
         ap.min_len = kAttnTcMaxLen + 1;
-        BBH_CUDA(launch_attention_long(ap, 2 * ws->num_sms, s));
+        BBH_CUDA(launch_attention_long(ap, 2 * ws->num_sms, s, ws->pdl));
       }
     }
     {
       KernelMark km(ws, s, 3);
-      BBH_CUDA(launch_gemm(P[1], s));
+      BBH_CUDA(launch_gemm(P[1], s, ws->pdl));
     }
     if (ws->fused_ffn) {
       KernelMark km(ws, s, 7);
-      BBH_CUDA(launch_mlp(ws->mlp_plans[size_t(l)], s));
+      BBH_CUDA(launch_mlp(ws->mlp_plans[size_t(l)], s, ws->pdl));
     } else {
       for (int j = 2; j < 4; ++j) {
         KernelMark km(ws, s, 2 + j);
-        BBH_CUDA(launch_gemm(P[j], s));
+        BBH_CUDA(launch_gemm(P[j], s, ws->pdl));
       }
     }
     if (dump) BBH_CUDA(cudaMemcpyAsync(dump + plane * (l + 1), ws->X, plane * 2, cudaMemcpyDeviceToDevice, s));
@@ -453,7 +454,7 @@ int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh
   if (pool) {
     int grid = ws->max_batch < ws->num_sms * 8 ? ws->max_batch : ws->num_sms * 8;
     KernelMark km(ws, s, 6);
-    BBH_CUDA(launch_pool_l2(pp, grid, s));
+    BBH_CUDA(launch_pool_l2(pp, grid, s, ws->pdl));
   }
   return BBH_OK;
 }
@@ -637,6 +638,15 @@ void bbh_ws_free(bbh_ws* ws) {
   cudaFree(ws->arena);
   cudaSetDevice(prev);
   delete ws;
+}
+
+int bbh_ws_set_pdl(bbh_ws* ws, int enable) {
+  if (!ws) return fail(BBH_ERR_ARG, "null workspace");
+  if ((enable != 0) != ws->pdl) {
+    ws->pdl = enable != 0;
+    drop_graph(ws);
+  }
+  return BBH_OK;
 }
 
 int bbh_ws_set_corpus_lanes(bbh_ws* ws, int lanes) {

@@ -36,6 +36,13 @@ constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // 4 s
 // nanoseconds pass, so waiters do not spin on the issue slots the working warps need.
 constexpr unsigned int kSuspendHintNs = 1000000u;  // 1 ms
 
+// Programmatic dependent launch: let the next kernel of the stream start launching (its
+// CTAs take SMs as they free up and run their prologue), and wait until the previous
+// kernel has completed and its memory is visible. No-ops for launches without the
+// programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

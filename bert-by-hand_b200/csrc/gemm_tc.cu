@@ -138,8 +138,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
   const unsigned long long trace_g0 = globaltimer();
 #endif
 
-  const int rows = p.rows_dev ? *p.rows_dev : p.rows;
-  const int m_tiles = (rows + Cfg::BM - 1) / Cfg::BM;
+  pdl_launch_dependents();
+  int rows = 0, m_tiles = 0;  // read after the wait for the previous kernel (below)
   const int n_tiles = (p.N + BN - 1) / BN;
   const int k_blocks = (p.K + Cfg::BK - 1) / Cfg::BK;
   // Tile schedule. Plain: tiles (m, n) in n-fastest order over all CTAs. Cluster: each
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
   const int crank = Cfg::CLUSTER > 1 ? static_cast<int>(cluster_ctarank()) : 0;
   const int first_tile = Cfg::CLUSTER > 1 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
   const int tile_step = Cfg::CLUSTER > 1 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
-  const int num_tiles = Cfg::CLUSTER > 1 ? m_tiles : m_tiles * n_tiles;
+  int num_tiles = 0;  // set once the row count is known
   auto tile_m0 = [&](int t) { return (Cfg::CLUSTER > 1 ? t : t / n_tiles) * Cfg::BM; };
   auto tile_n0 = [&](int t) { return Cfg::CLUSTER > 1 ? crank * BN : (t % n_tiles) * BN; };
 
@@ -182,6 +182,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
       s_beta[i] = __half2float(p.beta[i]);
     }
   }
+  // everything above touches only this kernel's own state and the weights; the
+  // activations and the row count come from the previous kernel
+  pdl_wait();
+  rows = p.rows_dev ? *p.rows_dev : p.rows;
+  m_tiles = (rows + Cfg::BM - 1) / Cfg::BM;
+  num_tiles = Cfg::CLUSTER > 1 ? m_tiles : m_tiles * n_tiles;
   tc_fence_before();
   __syncthreads();
   if constexpr (Cfg::CLUSTER > 1) cluster_sync_all();  // peers' barriers are initialised
@@ -448,7 +454,7 @@ int encode_2d(CUtensorMap* map, const __half* base, int rows, int cols, int ld, 
 }
 
 template <int BN, int EPI>
-static cudaError_t launch_inst(const GemmPlan& plan, cudaStream_t stream) {
+static cudaError_t launch_inst(const GemmPlan& plan, cudaStream_t stream, bool pdl) {
   using Cfg = GemmCfg<BN, EPI>;
   static bool attr_set[64] = {};
   static int max_clusters[64] = {};
@@ -483,22 +489,11 @@ static cudaError_t launch_inst(const GemmPlan& plan, cudaStream_t stream) {
     const int m_tiles_cap = (plan.rows_cap + Cfg::BM - 1) / Cfg::BM;
     int nclusters = dev < 64 ? max_clusters[dev] : 64;
     if (nclusters > m_tiles_cap) nclusters = m_tiles_cap;
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = Cfg::CLUSTER;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(Cfg::CLUSTER * nclusters);
-    cfg.blockDim = dim3(Cfg::THREADS);
-    cfg.dynamicSmemBytes = Cfg::SMEM;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, plan.tmA, plan.tmB, plan.tmC, plan.tmR, plan.p);
+    return launch_ex(kern, dim3(Cfg::CLUSTER * nclusters), dim3(Cfg::THREADS), Cfg::SMEM, stream, pdl, Cfg::CLUSTER,
+                     plan.tmA, plan.tmB, plan.tmC, plan.tmR, plan.p);
   } else {
-    kern<<<plan.grid, Cfg::THREADS, Cfg::SMEM, stream>>>(plan.tmA, plan.tmB, plan.tmC, plan.tmR, plan.p);
-    return cudaGetLastError();
+    return launch_ex(kern, dim3(plan.grid), dim3(Cfg::THREADS), Cfg::SMEM, stream, pdl, 1, plan.tmA, plan.tmB,
+                     plan.tmC, plan.tmR, plan.p);
   }
 }
 
@@ -548,16 +543,16 @@ int set_gemm_residual(GemmPlan* plan, const __half* R, int ldr) {
   return encode_2d(&plan->tmR, R, plan->rows_cap, plan->p.N, ldr, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream) {
+cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream, bool pdl) {
   if (plan.epi == kEpiResLN && !plan.p.residual) return cudaErrorInvalidValue;
   switch (plan.epi * 1000 + plan.bn) {
-    case kEpiBias * 1000 + 128: return launch_inst<128, kEpiBias>(plan, stream);
-    case kEpiGelu * 1000 + 128: return launch_inst<128, kEpiGelu>(plan, stream);
-    case kEpiBias * 1000 + 192: return launch_inst<192, kEpiBias>(plan, stream);
-    case kEpiGelu * 1000 + 192: return launch_inst<192, kEpiGelu>(plan, stream);
-    case kEpiBias * 1000 + 256: return launch_inst<256, kEpiBias>(plan, stream);
-    case kEpiGelu * 1000 + 256: return launch_inst<256, kEpiGelu>(plan, stream);
-    case kEpiResLN * 1000 + 192: return launch_inst<192, kEpiResLN>(plan, stream);
+    case kEpiBias * 1000 + 128: return launch_inst<128, kEpiBias>(plan, stream, pdl);
+    case kEpiGelu * 1000 + 128: return launch_inst<128, kEpiGelu>(plan, stream, pdl);
+    case kEpiBias * 1000 + 192: return launch_inst<192, kEpiBias>(plan, stream, pdl);
+    case kEpiGelu * 1000 + 192: return launch_inst<192, kEpiGelu>(plan, stream, pdl);
+    case kEpiBias * 1000 + 256: return launch_inst<256, kEpiBias>(plan, stream, pdl);
+    case kEpiGelu * 1000 + 256: return launch_inst<256, kEpiGelu>(plan, stream, pdl);
+    case kEpiResLN * 1000 + 192: return launch_inst<192, kEpiResLN>(plan, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

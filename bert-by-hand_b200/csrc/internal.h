@@ -11,6 +11,34 @@ struct bbh_ws;
 
 namespace bbh {
 
+// Launch with optional programmatic dependent launch (pdl) and cluster dimension.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                      int cluster, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cluster > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = static_cast<unsigned>(na);
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ------------------------------------------------------------------ C ABI internals
 // Sets the calling thread's bbh_last_error() message and returns code.
 int internal_fail(int code, const std::string& msg);
@@ -68,7 +96,7 @@ int encode_2d(CUtensorMap* map, const __half* base, int rows, int cols, int ld, 
               CUtensorMapSwizzle swz);
 // kEpiResLN: the residual [rows_cap, N] with row stride ldr (read with TMA, 16-byte aligned).
 int set_gemm_residual(GemmPlan* plan, const __half* R, int ldr);
-cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream);
+cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream, bool pdl = false);
 
 // ------------------------------------------------------------------ fused FFN block
 // out = LayerNorm(GELU(Y W1^T + b1) W2^T + b2 + residual) * gamma + beta (mlp_fused.cu)
@@ -96,7 +124,7 @@ struct MlpPlan {
 // Y: [rows_cap, 384] input (also the default residual); W1/W2 nn.Linear layouts; C output.
 int make_mlp_plan(MlpPlan* plan, const __half* Y, int rows_cap, const __half* W1, const __half* W2, __half* C,
                   int num_sms);
-cudaError_t launch_mlp(const MlpPlan& plan, cudaStream_t stream);
+cudaError_t launch_mlp(const MlpPlan& plan, cudaStream_t stream, bool pdl = false);
 
 // ------------------------------------------------------------------ other kernels
 // Forward-call description consumed by the first kernel of a forward. It is passed by
@@ -124,7 +152,7 @@ struct EmbedParams {
   int32_t* ws_meta;           // {B, T, max_len, has_mask}
   int* err;
 };
-cudaError_t launch_embed_ln(const EmbedParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_embed_ln(const EmbedParams& p, int grid, cudaStream_t stream, bool pdl = false);
 
 struct AttnParams {
   const __half* qkv;       // [T, 1152]: Q | K | V, head h at columns h*32
@@ -138,10 +166,10 @@ struct AttnParams {
   float scale_log2;        // log2(e) / sqrt(head_dim)
 };
 // tcgen05 flash-style kernel for sentences of kAttnTcMaxLen+1 .. 512 tokens (min_len)
-cudaError_t launch_attention_long(const AttnParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_attention_long(const AttnParams& p, int grid, cudaStream_t stream, bool pdl = false);
 // tcgen05 kernel: sentences of at most kAttnTcMaxLen tokens
 constexpr int kAttnTcMaxLen = 128;
-cudaError_t launch_attention_tc(const AttnParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_attention_tc(const AttnParams& p, int grid, cudaStream_t stream, bool pdl = false);
 
 struct PoolParams {
   const __half* hidden;    // [T, 384]
@@ -153,7 +181,7 @@ struct PoolParams {
 };
 const void* embed_kernel_fn();
 const void* pool_kernel_fn();
-cudaError_t launch_pool_l2(const PoolParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_pool_l2(const PoolParams& p, int grid, cudaStream_t stream, bool pdl = false);
 
 cudaError_t launch_layernorm(const __half* x, const __half* residual, const __half* gamma, const __half* beta,
                              __half* y, int rows, float eps, cudaStream_t stream);

@@ -101,8 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   long long trace_acc[12] = {};
   const long long trace_t0 = clock64();
 #endif
-  const int rows = p.rows_dev ? *p.rows_dev : p.rows;
-  const int m_tiles = (rows + kBM - 1) / kBM;
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSlots; ++s) {
@@ -130,6 +129,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     s_gamma[i] = __half2float(p.gamma[i]);
     s_beta[i] = __half2float(p.beta[i]);
   }
+  pdl_wait();  // the activations and the row count come from the previous kernel
+  const int rows = p.rows_dev ? *p.rows_dev : p.rows;
+  const int m_tiles = (rows + kBM - 1) / kBM;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -451,7 +453,7 @@ int make_mlp_plan(MlpPlan* plan, const __half* Y, int rows_cap, const __half* W1
   return BBH_OK;
 }
 
-cudaError_t launch_mlp(const MlpPlan& plan, cudaStream_t stream) {
+cudaError_t launch_mlp(const MlpPlan& plan, cudaStream_t stream, bool pdl) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -460,8 +462,8 @@ cudaError_t launch_mlp(const MlpPlan& plan, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  mlp_fused_kernel<<<plan.grid, kThreads, kSmem, stream>>>(plan.tmX, plan.tmW1, plan.tmW2, plan.p);
-  return cudaGetLastError();
+  return launch_ex(mlp_fused_kernel, dim3(plan.grid), dim3(kThreads), kSmem, stream, pdl, 1, plan.tmX, plan.tmW1,
+                   plan.tmW2, plan.p);
 }
 
 }  // namespace bbh

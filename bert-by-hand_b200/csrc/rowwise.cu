@@ -63,6 +63,8 @@ __device__ __forceinline__ void warp_layernorm12(float* f, const __half* gamma, 
 // padded length in padded mode). Also publishes the forward's segment table, per-token
 // key/pool mask and {B, T, max_len} for the later kernels, and validates the inputs.
 __global__ void __launch_bounds__(kRowThreads) embed_ln_kernel(EmbedParams p) {
+  pdl_launch_dependents();
+  pdl_wait();  // the previous forward's last kernels still read the buffers written here
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -146,9 +148,8 @@ __global__ void __launch_bounds__(kRowThreads) embed_ln_kernel(EmbedParams p) {
   }
 }
 
-cudaError_t launch_embed_ln(const EmbedParams& p, int grid, cudaStream_t stream) {
-  embed_ln_kernel<<<grid, kRowThreads, 0, stream>>>(p);
-  return cudaGetLastError();
+cudaError_t launch_embed_ln(const EmbedParams& p, int grid, cudaStream_t stream, bool pdl) {
+  return launch_ex(embed_ln_kernel, dim3(grid), dim3(kRowThreads), 0, stream, pdl, 1, p);
 }
 
 // --------------------------------------------------------------------------------------
@@ -162,6 +163,8 @@ __global__ void __launch_bounds__(kRowThreads) pool_l2_kernel(PoolParams p) {
   __shared__ int cnt[kRowThreads / 32];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  pdl_launch_dependents();
+  pdl_wait();  // the hidden states come from the previous kernel
   const int batch = p.meta ? p.meta[0] : p.batch;
   for (int b = blockIdx.x; b < batch; b += gridDim.x) {
     const int start = p.cu[b];
@@ -216,9 +219,8 @@ __global__ void __launch_bounds__(kRowThreads) pool_l2_kernel(PoolParams p) {
 const void* embed_kernel_fn() { return reinterpret_cast<const void*>(embed_ln_kernel); }
 const void* pool_kernel_fn() { return reinterpret_cast<const void*>(pool_l2_kernel); }
 
-cudaError_t launch_pool_l2(const PoolParams& p, int grid, cudaStream_t stream) {
-  pool_l2_kernel<<<grid, kRowThreads, 0, stream>>>(p);
-  return cudaGetLastError();
+cudaError_t launch_pool_l2(const PoolParams& p, int grid, cudaStream_t stream, bool pdl) {
+  return launch_ex(pool_l2_kernel, dim3(grid), dim3(kRowThreads), 0, stream, pdl, 1, p);
 }
 
 // --------------------------------------------------------------------------------------

@@ -86,6 +86,11 @@ BBH_API void bbh_ws_free(bbh_ws* ws);
  * through an HBM intermediate, as the reference's ffn_block -- currently the faster of the
  * two on B200 (the fused kernel's 128-wide 1-SM tiles use the tensor cores less well). */
 BBH_API int bbh_ws_set_ffn_fusion(bbh_ws* ws, int enable);
+/* 1 (default): the forward's kernels launch with programmatic dependent launch -- each
+ * kernel lets the next one start its launch and prologue (barrier set-up, tensor-memory
+ * allocation, weight staging) while it finishes, and the next one waits for its results
+ * before touching them; 0: plain stream order. Results are identical either way. */
+BBH_API int bbh_ws_set_pdl(bbh_ws* ws, int enable);
 /* 1 (default): bbh_embed* replay one captured CUDA graph per workspace; 0: eager launches. */
 BBH_API int bbh_ws_set_graph(bbh_ws* ws, int enable);
 /* Synchronises the device, returns the workspace's device error code (0 = none) and

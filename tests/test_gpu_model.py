@@ -254,3 +254,28 @@ def test_fused_ffn_matches_two_gemm_path(gw0):
     assert ws.device_error() == 0
     assert cos_rows(fused, plain).min() >= 0.99995
     assert np.abs(fused - plain).max() < 5e-3
+
+
+def test_pdl_bit_identical(gw0):
+    """Programmatic dependent launch changes when kernels start, not what they compute:
+    graph and eager forwards with and without it are bit-identical."""
+    import bbh
+    import synthetic as sy
+
+    lengths = sy.lengths_uniform(300, 8, 200, 6)
+    c = sy.bucketed_corpus(lengths, 300, 6)
+    b = c.batches[0]
+    d = lambda a: torch.as_tensor(np.asarray(a), dtype=torch.int32, device=DEV)
+    ids, types, cu = d(c.ids), d(c.types), d(b.cu)
+    outs = []
+    for pdl in (True, False):
+        for graph in (True, False):
+            ws = bbh.Workspace(gw0, b.tokens, 300, 256)
+            ws.set_pdl(pdl)
+            ws.set_graph(graph)
+            for _ in range(2):
+                e = ws.embed_varlen(ids, types, cu, b.max_len)
+            outs.append(e.cpu().numpy().view(np.uint16))
+            assert ws.device_error() == 0
+    for o in outs[1:]:
+        assert np.array_equal(o, outs[0])
