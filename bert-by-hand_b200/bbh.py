@@ -47,6 +47,7 @@ _SIGS = {
     "bbh_ws_set_graph": (_I, [_P, _I]),
     "bbh_ws_set_ffn_fusion": (_I, [_P, _I]),
     "bbh_ws_set_pdl": (_I, [_P, _I]),
+    "bbh_set_gemm_pairs": (_I, [_I]),
     "bbh_device_error": (_I, [_P, _I]),
     "bbh_launches_per_forward": (_I, [_P]),
     "bbh_ws_set_kernel_timing": (_I, [_P, _I]),
@@ -407,6 +408,13 @@ def spearman(x, y) -> float:
 
 
 # ---- unit operators ---------------------------------------------------------------------
+def set_gemm_pairs(mode: int) -> None:
+    """Tile shape of the bias / GELU projections in plans built from now on (process-wide):
+    0 = one SM per 128-row tile, 1 = SM pairs (256 x 192 where N allows, else 256 x 256),
+    2 = SM pairs, 256 x 256 first."""
+    _check(lib().bbh_set_gemm_pairs(int(mode)))
+
+
 def linear(A, W, bias=None, gelu=False, stream=None):
     """launch_matmul: A [M,K] @ W[N,K]^T (+bias) (+gelu) on the tcgen05 GEMM."""
     M, K = A.shape

@@ -664,6 +664,12 @@ int bbh_ws_set_ffn_fusion(bbh_ws* ws, int enable) {
   return BBH_OK;
 }
 
+int bbh_set_gemm_pairs(int mode) {
+  if (mode < 0 || mode > 2) return fail(BBH_ERR_ARG, "bbh_set_gemm_pairs: mode must be 0, 1 or 2");
+  bbh::g_gemm_pair_mode = mode;
+  return BBH_OK;
+}
+
 int bbh_ws_set_graph(bbh_ws* ws, int enable) {
   if (!ws) return fail(BBH_ERR_ARG, "null workspace");
   ws->use_graph = enable != 0;

@@ -521,6 +521,18 @@ int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const
   rc = encode_2d(&plan->tmC, C, rows_cap, N, ldc, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   plan->bn = bn;
+  plan->bn2 = 0;
+  memset(&plan->tmB2, 0, sizeof(plan->tmB2));
+  if (g_gemm_pair_mode) {
+    const int order[2] = {g_gemm_pair_mode == 2 ? 256 : 192, g_gemm_pair_mode == 2 ? 192 : 256};
+    for (int b2 : order)
+      if (gemm_pair_supported(N, epi, b2)) {
+        rc = encode_2d(&plan->tmB2, W, N, K, K, 64, b2 / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+        plan->bn2 = b2;
+        break;
+      }
+  }
   plan->epi = epi;
   plan->rows_cap = rows_cap;
   const int tiles_cap = ((rows_cap + 127) / 128) * ((N + bn - 1) / bn);
@@ -543,8 +555,11 @@ int set_gemm_residual(GemmPlan* plan, const __half* R, int ldr) {
   return encode_2d(&plan->tmR, R, plan->rows_cap, plan->p.N, ldr, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+int g_gemm_pair_mode = 1;
+
 cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream, bool pdl) {
   if (plan.epi == kEpiResLN && !plan.p.residual) return cudaErrorInvalidValue;
+  if (plan.bn2) return launch_gemm_pair(plan, stream, pdl);
   switch (plan.epi * 1000 + plan.bn) {
     case kEpiBias * 1000 + 128: return launch_inst<128, kEpiBias>(plan, stream, pdl);
     case kEpiGelu * 1000 + 128: return launch_inst<128, kEpiGelu>(plan, stream, pdl);

@@ -78,8 +78,10 @@ struct GemmPlan {
   CUtensorMap tmB;
   CUtensorMap tmC;
   CUtensorMap tmR;  // residual (kEpiResLN), set by set_gemm_residual
+  CUtensorMap tmB2;  // W with (bn2 / 2)-row boxes for the CTA-pair kernel
   GemmParams p;
   int bn;
+  int bn2;  // pair-tile width (CTA-pair kernel, gemm_pair.cu) or 0 for the one-SM kernel
   int epi;
   int grid;
   int rows_cap;
@@ -97,6 +99,12 @@ int encode_2d(CUtensorMap* map, const __half* base, int rows, int cols, int ld, 
 // kEpiResLN: the residual [rows_cap, N] with row stride ldr (read with TMA, 16-byte aligned).
 int set_gemm_residual(GemmPlan* plan, const __half* R, int ldr);
 cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream, bool pdl = false);
+// CTA-pair kernel (gemm_pair.cu): bias / GELU epilogues, N a multiple of the pair width.
+bool gemm_pair_supported(int N, int epi, int bn);
+cudaError_t launch_gemm_pair(const GemmPlan& plan, cudaStream_t stream, bool pdl);
+// Which kernel plans built from now on use for the bias / GELU GEMMs: 0 = one-SM tiles,
+// 1 = CTA pairs of 256 x 192 tiles where N allows it, else 256 x 256, 2 = 256 x 256 first.
+extern int g_gemm_pair_mode;
 
 // ------------------------------------------------------------------ fused FFN block
 // out = LayerNorm(GELU(Y W1^T + b1) W2^T + b2 + residual) * gamma + beta (mlp_fused.cu)

@@ -91,6 +91,11 @@ BBH_API int bbh_ws_set_ffn_fusion(bbh_ws* ws, int enable);
  * allocation, weight staging) while it finishes, and the next one waits for its results
  * before touching them; 0: plain stream order. Results are identical either way. */
 BBH_API int bbh_ws_set_pdl(bbh_ws* ws, int enable);
+/* Tile shape of the bias and GELU projections (QKV, first FFN layer) in plans built after
+ * the call (workspaces created and unit operations called later): 0 = one SM per 128-row
+ * tile; 1 (default) = pairs of SMs sharing one 256-row tile (tcgen05 cta_group::2),
+ * 192 columns wide where N allows, else 256; 2 = pairs, 256 columns first. Process-wide. */
+BBH_API int bbh_set_gemm_pairs(int mode);
 /* 1 (default): bbh_embed* replay one captured CUDA graph per workspace; 0: eager launches. */
 BBH_API int bbh_ws_set_graph(bbh_ws* ws, int enable);
 /* Synchronises the device, returns the workspace's device error code (0 = none) and
