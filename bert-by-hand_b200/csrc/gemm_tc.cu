@@ -79,28 +79,6 @@ struct GemmCfg {
 };
 
 
-__device__ __forceinline__ void ln_add32(float* v, const float* bias, const uint4* res4) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float r8[8];
-    unpack_half8(res4[j], r8);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) v[j * 8 + e] += bias[j * 8 + e] + r8[e];
-  }
-}
-
-__device__ __forceinline__ void ln_pack32(const float* v, int col0, float mean, float rstd, const float* gamma,
-                                          const float* beta, uint32_t* w) {
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const float4 g = *reinterpret_cast<const float4*>(gamma + col0 + 4 * q);
-    const float4 b = *reinterpret_cast<const float4*>(beta + col0 + 4 * q);
-    const float* x = v + 4 * q;
-    w[2 * q] = pack_half2((x[0] - mean) * rstd * g.x + b.x, (x[1] - mean) * rstd * g.y + b.y);
-    w[2 * q + 1] = pack_half2((x[2] - mean) * rstd * g.z + b.z, (x[3] - mean) * rstd * g.w + b.w);
-  }
-}
-
 template <int BN, int EPI>
 __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -271,20 +249,16 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
     const int quad = warp & 3;        // TMEM lane quadrant this warp may access
     const int half = (warp - 2) >> 2;  // which column part of the tile (0 .. PARTS-1)
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const int rloc = quad * 32 + lane;  // row within the tile
     ChunkStore cst{s_stage + (warp - 2) * 4096, &tmC, lane};
     int acc = 0;
     uint32_t acc_phase = 0;
     int iter = 0;  // tiles processed by this CTA (peer-statistics slot and phase)
     const int we = warp - 2;  // epilogue warp index
-    // LayerNorm: the warp's 32 x 64 residual slice of a tile is TMA-loaded into its staging
-    // buffer (the output chunk has the same shape and is written back in place), one tile
-    // ahead: the load for tile i+1 is issued as soon as tile i's store has read the buffer.
+    // LayerNorm: the residual slice of the first tile is queued before the loop
+    const LnSlice ln{cst.buf, &tmC, &tmR, &res_bar[we], red, xstat, xfull_bar,
+                     static_cast<uint32_t>(crank ^ 1), s_bias, s_gamma, s_beta, p.eps, lane, quad, half, we};
     if constexpr (EPI == kEpiResLN) {
-      if (lane == 0 && first_tile < num_tiles) {
-        mbar_arrive_expect_tx(&res_bar[we], 4096);
-        tma_load_2d(cst.buf, &tmR, &res_bar[we], tile_n0(first_tile) + half * HB, tile_m0(first_tile) + quad * 32);
-      }
+      if (first_tile < num_tiles) ln.prefetch(tile_n0(first_tile) + half * HB, tile_m0(first_tile) + quad * 32);
     }
     for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++iter) {
       const int m0 = tile_m0(tile);
@@ -300,79 +274,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
         float v[64];
         tmem_ld64(tacc, tacc + 32, v);
         warp_arrive(&acce_bar[acc]);
-        // the residual slice (swizzled rows in the staging buffer; lane = row)
-        if (!mbar_wait(&res_bar[we], iter & 1, abort_flag, p.err)) break;
-        uint8_t* rowp = cst.buf + lane * 128;
-        const int sw = lane & 7;
-        uint4 res[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) res[j] = *reinterpret_cast<const uint4*>(rowp + ((j ^ sw) << 4));
-        // v = acc + bias + residual; shifted sums (shift = this warp's first value)
-        ln_add32(v, s_bias + c0, &res[0]);
-        ln_add32(v + 32, s_bias + c0 + 32, &res[4]);
-        const float shift = v[0];
-        float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const float d = v[j] - shift;
-          s1 += d;
-          s2 += d * d;
-        }
-        // per-part mean and M2 combined over the PARTS warps of this quadrant
-        // (Chan et al.: M2 = sum M2_i + n * sum (mean_i - mean)^2, equal part sizes n).
-        // Two scratch slots alternate by tile, so one barrier per tile suffices: a warp can
-        // rewrite a slot only after every part has passed the next tile's barrier.
-        const int slot = iter & 1;
-        float* rs = red + slot * (2 * 3 * 128);
-        rs[half * 128 + rloc] = shift + s1 * (1.0f / HB);
-        rs[384 + half * 128 + rloc] = fmaxf(s2 - s1 * s1 * (1.0f / HB), 0.f);
-        named_barrier(1 + quad, 32 * Cfg::PARTS);
-        float mean_c = 0.f;
-#pragma unroll
-        for (int i = 0; i < Cfg::PARTS; ++i) mean_c += rs[i * 128 + rloc];
-        mean_c *= 1.0f / Cfg::PARTS;
-        float m2_c = 0.f;
-#pragma unroll
-        for (int i = 0; i < Cfg::PARTS; ++i) {
-          const float d = rs[i * 128 + rloc] - mean_c;
-          m2_c += rs[384 + i * 128 + rloc] + d * d * HB;
-        }
-        // exchange with the other CTA of the cluster (the other 192 columns): part-0 lanes
-        // send their row's (mean, M2) with st.async, which completes bytes on the peer's
-        // barrier; one thread per CTA posts the expected byte count on its own barrier.
-        // A slot is rewritten two tiles later, after every part of this quadrant has
-        // passed the next tile's barrier, so the receiver has read it by then.
-        if (half == 0) {
-          const uint32_t peer = static_cast<uint32_t>(crank ^ 1);
-          st_async_f32x2(mapa_shared(smem_u32(&xstat[slot * 128 + rloc]), peer), mean_c, m2_c,
-                         mapa_shared(smem_u32(&xfull_bar[slot]), peer));
-        }
-        if (we == 0 && lane == 0) mbar_arrive_expect_tx(&xfull_bar[slot], 128 * 8);
-        if (!mbar_wait_cluster(&xfull_bar[slot], (iter >> 1) & 1, abort_flag, p.err)) break;
-        const float2 ps = xstat[slot * 128 + rloc];
-        const float dp = mean_c - ps.x;
-        const float mean = 0.5f * (mean_c + ps.x);
-        const float m2 = m2_c + ps.y + dp * dp * (0.5f * BN);
-        const float rstd = rsqrtf(m2 * (1.0f / kHidden) + p.eps);
-        // normalise, affine, write the row back over its residual, store the chunk
-        uint32_t w[32];
-        ln_pack32(v, c0, mean, rstd, s_gamma, s_beta, w);
-        ln_pack32(v + 32, c0 + 32, mean, rstd, s_gamma, s_beta, w + 16);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<uint4*>(rowp + ((j ^ sw) << 4)) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-        fence_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmC, cst.buf, c0, row0);
-          bulk_commit();
-          const int nt = tile + tile_step;
-          if (nt < num_tiles) {
-            bulk_wait_read<0>();
-            mbar_arrive_expect_tx(&res_bar[we], 4096);
-            tma_load_2d(cst.buf, &tmR, &res_bar[we], tile_n0(nt) + half * HB, tile_m0(nt) + quad * 32);
-          }
-        }
+        const int nt = tile + tile_step;
+        if (!ln.finish(v, iter, c0, row0, nt < num_tiles, tile_n0(nt) + half * HB, tile_m0(nt) + quad * 32, abort_flag,
+                       p.err))
+          break;
       } else {
         const float* sb = bias_in_smem ? s_bias : nullptr;
         static_assert(HB % 64 == 0, "64-column output chunks");
