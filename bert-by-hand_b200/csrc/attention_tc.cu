@@ -276,13 +276,12 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(AttnParams 
         const uint32_t m = chunk_mask(ch);
         float t[32];
         tmem_ld32(trow + c_lo + ch * 32, t);
-        if (m == 0xffffffffu) {
+        if (m != 0xffffffffu) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) mq[j & 3] = fmaxf(mq[j & 3], t[j]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) mq[j & 3] = fmaxf(mq[j & 3], (m >> j) & 1u ? t[j] : -INFINITY);
+          for (int j = 0; j < 32; ++j) t[j] = (m >> j) & 1u ? t[j] : -INFINITY;
         }
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) mq[(j >> 1) & 3] = fmax3(mq[(j >> 1) & 3], t[j], t[j + 1]);
       }
       const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
       const float msc = mx == -INFINITY ? 0.f : mx * scale;
@@ -532,14 +531,14 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
         }
         mk = row_ok ? mm : 0u;
       }
-      float pmax = -INFINITY;
-      if (mk == 0xffffffffu) {
+      if (mk != 0xffffffffu) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) pmax = fmaxf(pmax, t[e]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) pmax = fmaxf(pmax, (mk >> e) & 1u ? t[e] : -INFINITY);
+        for (int e = 0; e < 32; ++e) t[e] = (mk >> e) & 1u ? t[e] : -INFINITY;
       }
+      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) mq[(e >> 1) & 3] = fmax3(mq[(e >> 1) & 3], t[e], t[e + 1]);
+      const float pmax = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
       sm.part[half][row] = pmax;
       __syncthreads();
       const float bmax = fmaxf(pmax, sm.part[half ^ 1][row]);

@@ -428,6 +428,13 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
          (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// max(a, b, c) in one instruction (three-operand max.f32, sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // ---------------------------------------------------------------- warp utils
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
