@@ -217,6 +217,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--lanes", type=int, default=2, choices=[1, 2],
                     help="compute lanes: alternate batches over this many workspaces / streams")
+    ap.add_argument("--gemm-pairs", type=int, default=1, choices=[0, 1, 2],
+                    help="GEMM tiles: 0 = one SM per 128-row tile, 1 = SM pairs 256x192 (default), "
+                         "2 = SM pairs 256x256 where N allows")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -239,6 +242,7 @@ def main():
     desc, layers, packed, spec, per_gpu, batch = WORKLOADS[args.workload]
     n = args.sentences or per_gpu
     weights = sy.random_weights(0, layers)
+    bbh.set_gemm_pairs(args.gemm_pairs)
     gw = bbh.ModelWeights.from_numpy(weights, layers, local)
 
     lengths = make_lengths(spec, n, seed=3 + 7919 * rank)
@@ -452,6 +456,7 @@ def main():
                 "l2": "inputs larger than L2 (each step streams ~1 GB of activations per GPU)",
                 "graph": "one CUDA graph per workspace, re-pointed per batch",
                 "lanes": f"{args.lanes} (batches alternate over {args.lanes} workspaces / streams)",
+                "gemm_tiles": ["one SM per 128-row tile", "SM pairs, 256x192", "SM pairs, 256x256 where N allows"][args.gemm_pairs],
             },
             "roofline": roofline,
             "kernels": per_kernel,
