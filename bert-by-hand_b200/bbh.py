@@ -64,6 +64,7 @@ _SIGS = {
     "bbh_mean_pool_l2": (_I, [_P, _P, _P, _I, _P, _P]),
     "bbh_plan_batches": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, ctypes.POINTER(_I)]),
     "bbh_embed_corpus": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _P, _P]),
+    "bbh_embed_padded": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
     "bbh_ws_set_corpus_lanes": (_I, [_P, _I]),
     "bbh_vocab_load": (_I, [ctypes.c_char_p, _I, ctypes.POINTER(_P)]),
     "bbh_vocab_free": (None, [_P]),
@@ -285,6 +286,23 @@ class Workspace:
         _check(lib().bbh_embed_corpus(self.handle, self.weights.handle, p(ids), p(types), p(offsets), n,
                                       p(plan.order), p(plan.batch_first), p(plan.batch_rank), plan.n_batches,
                                       rank, p(out), _stream(stream)))
+        return out
+
+    def embed_padded(self, ids, types, mask, batch: int, out=None, stream=None):
+        """The padded bench loop from HOST numpy arrays: ids/types/mask int32 [n, seq]
+        (types / mask may be None), batches of `batch` consecutive sentences with pipelined
+        staging; returns the fp16 [n, 384] host array."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        n, seq = ids.shape
+        types = None if types is None else np.ascontiguousarray(types, dtype=np.int32).reshape(n, seq)
+        mask = None if mask is None else np.ascontiguousarray(mask, dtype=np.int32).reshape(n, seq)
+        if out is None:
+            out = np.zeros((n, HIDDEN), dtype=np.float16)
+        if out.dtype != np.float16 or out.shape != (n, HIDDEN) or not out.flags.c_contiguous:
+            raise ValueError("out must be a contiguous float16 [n, 384] host array")
+        p = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+        _check(lib().bbh_embed_padded(self.handle, self.weights.handle, p(ids), p(types), p(mask), n, seq, int(batch),
+                                      p(out), _stream(stream)))
         return out
 
     def free(self):

@@ -27,9 +27,9 @@ namespace {
 double sentence_work(int64_t L) { return 3538944.0 * double(L) + 1536.0 * double(L) * double(L); }
 
 struct Slot {
-  int32_t *h_ids = nullptr, *h_types = nullptr, *h_cu = nullptr;  // pinned
-  uint16_t* h_emb = nullptr;                                      // pinned
-  int32_t *d_ids = nullptr, *d_types = nullptr, *d_cu = nullptr;
+  int32_t *h_ids = nullptr, *h_types = nullptr, *h_cu = nullptr, *h_mask = nullptr;  // pinned
+  uint16_t* h_emb = nullptr;                                                         // pinned
+  int32_t *d_ids = nullptr, *d_types = nullptr, *d_cu = nullptr, *d_mask = nullptr;
   uint16_t* d_emb = nullptr;
   cudaEvent_t h2d = nullptr, fwd = nullptr, d2h = nullptr;
   int batch = -1;  // plan batch whose results the slot holds (-1: none)
@@ -60,10 +60,12 @@ void free_stage(void* p) {
     cudaFreeHost(s.h_ids);
     cudaFreeHost(s.h_types);
     cudaFreeHost(s.h_cu);
+    cudaFreeHost(s.h_mask);
     cudaFreeHost(s.h_emb);
     cudaFree(s.d_ids);
     cudaFree(s.d_types);
     cudaFree(s.d_cu);
+    cudaFree(s.d_mask);
     cudaFree(s.d_emb);
     for (cudaEvent_t e : {s.h2d, s.fwd, s.d2h})
       if (e) cudaEventDestroy(e);
@@ -93,9 +95,11 @@ int make_stage(bbh_ws* ws, Stage** out) {
     ok = ok && cudaHostAlloc(&s.h_ids, tok, cudaHostAllocDefault) == cudaSuccess &&
          cudaHostAlloc(&s.h_types, tok, cudaHostAllocDefault) == cudaSuccess &&
          cudaHostAlloc(&s.h_cu, cu, cudaHostAllocDefault) == cudaSuccess &&
+         cudaHostAlloc(&s.h_mask, tok, cudaHostAllocDefault) == cudaSuccess &&
          cudaHostAlloc(&s.h_emb, emb, cudaHostAllocDefault) == cudaSuccess &&
          cudaMalloc(&s.d_ids, tok) == cudaSuccess && cudaMalloc(&s.d_types, tok) == cudaSuccess &&
-         cudaMalloc(&s.d_cu, cu) == cudaSuccess && cudaMalloc(&s.d_emb, emb) == cudaSuccess &&
+         cudaMalloc(&s.d_cu, cu) == cudaSuccess && cudaMalloc(&s.d_mask, tok) == cudaSuccess &&
+         cudaMalloc(&s.d_emb, emb) == cudaSuccess &&
          cudaEventCreateWithFlags(&s.h2d, cudaEventDisableTiming) == cudaSuccess &&
          cudaEventCreateWithFlags(&s.fwd, cudaEventDisableTiming) == cudaSuccess &&
          cudaEventCreateWithFlags(&s.d2h, cudaEventDisableTiming) == cudaSuccess;
@@ -106,6 +110,43 @@ int make_stage(bbh_ws* ws, Stage** out) {
     return bbh::internal_fail(BBH_ERR_CUDA, "bbh_embed_corpus: staging allocation failed");
   }
   *out = st;
+  return BBH_OK;
+}
+
+// The workspace's staging (created on first use, freed with the workspace) and, for two
+// lanes, its second workspace and stream. Switches to the workspace's device; *prev gets
+// the caller's.
+int acquire_stage(bbh_ws* ws, const bbh_weights* w, Stage** out, int* prev, const char* who) {
+  int device = 0, max_tokens = 0, max_batch = 0, max_len = 0;
+  bbh::ws_limits(ws, &device, &max_tokens, &max_batch, &max_len);
+  cudaGetDevice(prev);
+  if (cudaSetDevice(device) != cudaSuccess) return bbh::internal_fail(BBH_ERR_CUDA, std::string(who) + ": cudaSetDevice");
+  void** slotp = bbh::ws_corpus_stage(ws, free_stage);
+  if (!*slotp) {
+    Stage* st = nullptr;
+    int rc = make_stage(ws, &st);
+    if (rc) return rc;
+    *slotp = st;
+  }
+  Stage& st = *static_cast<Stage*>(*slotp);
+  if (bbh::ws_corpus_lanes(ws) == 2 && !st.ws2) {
+    int rc = bbh_ws_create(w, max_tokens, max_batch, max_len, &st.ws2);
+    if (!rc && cudaStreamCreateWithFlags(&st.s2, cudaStreamNonBlocking) != cudaSuccess)
+      rc = bbh::internal_fail(BBH_ERR_CUDA, std::string(who) + ": stream creation failed");
+    if (rc) return rc;
+  }
+  *out = &st;
+  return BBH_OK;
+}
+
+// Device-detected input errors of the workspace(s) after a driver run.
+int device_status(bbh_ws* ws, const Stage& st, const char* who) {
+  int dev_err = bbh_device_error(ws, 0);
+  if (dev_err == 0 && st.ws2) dev_err = bbh_device_error(st.ws2, 0);
+  if (dev_err < 0) return dev_err;
+  if (dev_err > 0)
+    return bbh::internal_fail(BBH_ERR_DEVICE, std::string(who) + ": the device flagged bad input (code " +
+                                                  std::to_string(dev_err) + ")");
   return BBH_OK;
 }
 
@@ -197,30 +238,17 @@ int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const
                                                       " exceeds the workspace's token capacity");
   }
   int prev = 0;
-  cudaGetDevice(&prev);
-  if (cudaSetDevice(device) != cudaSuccess) return bbh::internal_fail(BBH_ERR_CUDA, "bbh_embed_corpus: cudaSetDevice");
-  void** slotp = bbh::ws_corpus_stage(ws, free_stage);
-  if (!*slotp) {
-    Stage* st = nullptr;
-    int rc = make_stage(ws, &st);
-    if (rc) {
+  Stage* stp = nullptr;
+  {
+    const int rc0 = acquire_stage(ws, w, &stp, &prev, "bbh_embed_corpus");
+    if (rc0) {
       cudaSetDevice(prev);
-      return rc;
+      return rc0;
     }
-    *slotp = st;
   }
-  Stage& st = *static_cast<Stage*>(*slotp);
+  Stage& st = *stp;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int lanes = bbh::ws_corpus_lanes(ws);
-  if (lanes == 2 && !st.ws2) {
-    int rc = bbh_ws_create(w, max_tokens, max_batch, max_len, &st.ws2);
-    if (!rc && cudaStreamCreateWithFlags(&st.s2, cudaStreamNonBlocking) != cudaSuccess)
-      rc = bbh::internal_fail(BBH_ERR_CUDA, "bbh_embed_corpus: stream creation failed");
-    if (rc) {
-      cudaSetDevice(prev);
-      return rc;
-    }
-  }
 
   // Copies a finished slot's embeddings to their corpus rows.
   auto drain = [&](Slot& sl) -> int {
@@ -288,15 +316,86 @@ int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const
     if (!rc) rc = r2;
     sl.batch = -1;
   }
-  if (!rc) {
-    int dev_err = bbh_device_error(ws, 0);
-    if (dev_err == 0 && st.ws2) dev_err = bbh_device_error(st.ws2, 0);
-    if (dev_err < 0)
-      rc = dev_err;
-    else if (dev_err > 0)
-      rc = bbh::internal_fail(BBH_ERR_DEVICE, "bbh_embed_corpus: the device flagged bad input (code " +
-                                                  std::to_string(dev_err) + ")");
+  if (!rc) rc = device_status(ws, st, "bbh_embed_corpus");
+  cudaSetDevice(prev);
+  return rc;
+}
+
+int bbh_embed_padded(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types, const int32_t* mask,
+                     int n, int seq, int batch, uint16_t* emb, void* stream) {
+  if (!ws || !w || n < 0 || seq <= 0 || batch <= 0 || (n > 0 && (!ids || !emb)))
+    return bbh::internal_fail(BBH_ERR_ARG, "bbh_embed_padded: bad arguments");
+  int device = 0, max_tokens = 0, max_batch = 0, max_len = 0;
+  bbh::ws_limits(ws, &device, &max_tokens, &max_batch, &max_len);
+  if (batch > max_batch || int64_t(batch) * seq > max_tokens || seq > max_len)
+    return bbh::internal_fail(BBH_ERR_CAPACITY, "bbh_embed_padded: batch x seq exceeds the workspace");
+  int prev = 0;
+  Stage* stp = nullptr;
+  {
+    const int rc0 = acquire_stage(ws, w, &stp, &prev, "bbh_embed_padded");
+    if (rc0) {
+      cudaSetDevice(prev);
+      return rc0;
+    }
   }
+  Stage& st = *stp;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int lanes = bbh::ws_corpus_lanes(ws);
+  // a slot's results are the consecutive rows [first, first + count) of emb
+  int first_of[2] = {0, 0}, count_of[2] = {0, 0};
+  auto drain = [&](int k) -> int {
+    Slot& sl = st.slot[k];
+    if (sl.batch < 0) return BBH_OK;
+    if (cudaEventSynchronize(sl.d2h) != cudaSuccess)
+      return bbh::internal_fail(BBH_ERR_CUDA, "bbh_embed_padded: device->host copy failed");
+    std::memcpy(emb + size_t(first_of[k]) * BBH_HIDDEN, sl.h_emb, size_t(count_of[k]) * BBH_HIDDEN * sizeof(uint16_t));
+    sl.batch = -1;
+    return BBH_OK;
+  };
+  int rc = BBH_OK;
+  int k = 0;
+  for (int b = 0, first = 0; first < n && rc == BBH_OK; ++b, first += batch) {
+    const int si = k & 1;
+    Slot& sl = st.slot[si];
+    bbh_ws* lws = (lanes == 2 && si) ? st.ws2 : ws;
+    cudaStream_t ls = (lanes == 2 && si) ? st.s2 : s;
+    ++k;
+    rc = drain(si);  // also guarantees the slot's buffers are no longer in use
+    if (rc) break;
+    const int count = std::min(batch, n - first);
+    const size_t off = size_t(first) * seq, tb = size_t(count) * seq * sizeof(int32_t);
+    std::memcpy(sl.h_ids, ids + off, tb);
+    if (types) std::memcpy(sl.h_types, types + off, tb);
+    if (mask) std::memcpy(sl.h_mask, mask + off, tb);
+    bool ok = cudaMemcpyAsync(sl.d_ids, sl.h_ids, tb, cudaMemcpyHostToDevice, st.up) == cudaSuccess &&
+              (!types || cudaMemcpyAsync(sl.d_types, sl.h_types, tb, cudaMemcpyHostToDevice, st.up) == cudaSuccess) &&
+              (!mask || cudaMemcpyAsync(sl.d_mask, sl.h_mask, tb, cudaMemcpyHostToDevice, st.up) == cudaSuccess) &&
+              cudaEventRecord(sl.h2d, st.up) == cudaSuccess && cudaStreamWaitEvent(ls, sl.h2d, 0) == cudaSuccess;
+    if (!ok) {
+      rc = bbh::internal_fail(BBH_ERR_CUDA, "bbh_embed_padded: host->device copy failed");
+      break;
+    }
+    rc = bbh_embed(lws, w, sl.d_ids, types ? sl.d_types : nullptr, mask ? sl.d_mask : nullptr, sl.d_emb, count, seq,
+                   ls);
+    if (rc) break;
+    ok = cudaEventRecord(sl.fwd, ls) == cudaSuccess && cudaStreamWaitEvent(st.down, sl.fwd, 0) == cudaSuccess &&
+         cudaMemcpyAsync(sl.h_emb, sl.d_emb, size_t(count) * BBH_HIDDEN * sizeof(uint16_t), cudaMemcpyDeviceToHost,
+                         st.down) == cudaSuccess &&
+         cudaEventRecord(sl.d2h, st.down) == cudaSuccess;
+    if (!ok) {
+      rc = bbh::internal_fail(BBH_ERR_CUDA, "bbh_embed_padded: device->host copy failed");
+      break;
+    }
+    sl.batch = b;
+    first_of[si] = first;
+    count_of[si] = count;
+  }
+  for (int i = 0; i < 2; ++i) {
+    const int r2 = drain(i);
+    if (!rc) rc = r2;
+    st.slot[i].batch = -1;
+  }
+  if (!rc) rc = device_status(ws, st, "bbh_embed_padded");
   cudaSetDevice(prev);
   return rc;
 }

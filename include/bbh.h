@@ -198,6 +198,15 @@ BBH_API int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* id
                              const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
                              const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb, void* stream);
 
+/* bbh_embed_padded: the reference's padded bench loop (bench/bench.cu:40-50: bert_embed
+ * over consecutive batches of a padded [n, seq] corpus) as one call. ids/types/mask are
+ * HOST int32 [n, seq] row-major (types / mask may be NULL: all 0 / all 1); batches of
+ * `batch` consecutive sentences (the last may be shorter) go through the same two pinned
+ * staging slots, copy streams and lanes as bbh_embed_corpus; emb is HOST fp16 [n, 384].
+ * batch x seq must fit the workspace (BBH_ERR_CAPACITY otherwise). */
+BBH_API int bbh_embed_padded(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
+                             const int32_t* mask, int n, int seq, int batch, uint16_t* emb, void* stream);
+
 /* ---- the step before the path: WordPiece tokenizer (host only) ---------------------------
  * The reference tokenizes with the HF tokenizer of its sentence-transformers model
  * (scripts/dump_corpus.py:34-38: BERT uncased, truncation=True, max_length=128) and has no

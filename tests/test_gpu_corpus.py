@@ -109,3 +109,34 @@ def test_two_lanes_bit_identical(setup):
     assert np.array_equal(one.view(np.uint16), two.view(np.uint16))
     with pytest.raises(bbh.BBHError):
         ws.set_corpus_lanes(3)
+
+
+@pytest.mark.parametrize("lanes", [1, 2])
+def test_padded_corpus_matches_per_batch_embed(setup, lanes):
+    """bbh_embed_padded (the reference's padded bench loop as one call, host arrays in and
+    out) gives exactly one bbh_embed per batch of consecutive sentences, last batch short."""
+    bbh, w, gw, *_ = setup
+    rng = np.random.default_rng(11)
+    n, seq, batch = 150, 48, 32
+    lens = rng.integers(3, seq + 1, size=n)
+    ids = rng.integers(1000, 30522, size=(n, seq)).astype(np.int32)
+    ids[:, 0] = 101
+    mask = (np.arange(seq)[None, :] < lens[:, None]).astype(np.int32)
+    ids[np.arange(n), lens - 1] = 102
+    ids *= mask
+    types = ((rng.random((n, seq)) < 0.3) * mask).astype(np.int32)
+    ws = bbh.Workspace(gw, batch * seq, batch, seq)
+    ws.set_corpus_lanes(lanes)
+    got = ws.embed_padded(ids, types, mask, batch)
+    ref = np.zeros_like(got)
+    d = lambda a: torch.as_tensor(a, dtype=torch.int32, device="cuda")
+    for f in range(0, n, batch):
+        sl = slice(f, min(n, f + batch))
+        ref[sl] = ws.embed(d(ids[sl]), d(types[sl]), d(mask[sl])).cpu().numpy()
+    assert ws.device_error() == 0
+    assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
+    norms = np.linalg.norm(got.astype(np.float32), axis=1)
+    assert np.all(np.abs(norms - 1) < 2e-3)
+    with pytest.raises(bbh.BBHError) as e:
+        ws.embed_padded(ids, types, mask, batch + 1)
+    assert e.value.code == -2
