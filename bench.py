@@ -363,7 +363,7 @@ def main():
         h_emb_np = np.zeros((n, 384), np.float16)
 
         def e2e_step():
-            # the reference's padded bench loop as one library call: pinned staging, copy
+            # bert_embed per batch of the padded host corpus as one library call: pinned staging, copy
             # streams and compute lanes inside bbh_embed_padded
             ws.embed_padded(host_ids, host_types, host_mask, batch, out=h_emb_np)
 

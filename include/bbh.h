@@ -198,8 +198,9 @@ BBH_API int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* id
                              const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
                              const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb, void* stream);
 
-/* bbh_embed_padded: the reference's padded bench loop (bench/bench.cu:40-50: bert_embed
- * over consecutive batches of a padded [n, seq] corpus) as one call. ids/types/mask are
+/* bbh_embed_padded: bert_embed (the call the reference's bench/bench.cu:44-49 repeats on
+ * device-resident inputs) over consecutive batches of a padded [n, seq] corpus held in host
+ * memory, as one call. ids/types/mask are
  * HOST int32 [n, seq] row-major (types / mask may be NULL: all 0 / all 1); batches of
  * `batch` consecutive sentences (the last may be shorter) go through the same two pinned
  * staging slots, copy streams and lanes as bbh_embed_corpus; emb is HOST fp16 [n, 384].
