@@ -160,6 +160,16 @@ inline void embed_corpus(Workspace& ws, const ModelWeights& w, const int32_t* id
                     "embed_corpus");
 }
 
+// bert_embed over consecutive batches of `batch` sentences of a padded host corpus:
+// ids/types/mask host [n, seq] (types / mask may be null); embedding host [n, 384] fp16.
+inline void embed_padded(Workspace& ws, const ModelWeights& w, const int32_t* ids, const int32_t* types,
+                         const int32_t* mask, int n, int seq, int batch, __half* embedding,
+                         cudaStream_t stream = nullptr) {
+  bbh_detail::check(bbh_embed_padded(ws.get(w), w.handle, ids, types, mask, n, seq, batch,
+                                     reinterpret_cast<uint16_t*>(embedding), stream),
+                    "embed_padded");
+}
+
 // WordPiece tokenization into the packed layout of bert_embed_varlen (host vectors).
 struct Tokenized {
   std::vector<int32_t> ids, cu_seqlens;
