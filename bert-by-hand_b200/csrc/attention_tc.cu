@@ -39,7 +39,7 @@ static_assert(sizeof(TcBuf) % 1024 == 0, "swizzled operands must stay 1024-byte 
 
 struct TcSmem {
   TcBuf buf[2];
-  uint8_t keyok[2][kTcRows];    // 1 = usable key row (padded calls with a token mask)
+  uint32_t keybits[2][kTcRows / 32];  // bit r: key row r usable (padded calls with a token mask)
   uint64_t bar_s, bar_o;
   uint32_t tmem;
   int abort_flag;
@@ -110,7 +110,7 @@ __device__ __forceinline__ TcItem tc_find(const int* cu, int batch, int item, in
 }
 
 __device__ __forceinline__ void tc_load(const AttnParams& p, const uint8_t* tokmask, const TcItem& u, TcBuf& B,
-                                        uint8_t* keyok, int tid) {
+                                        uint32_t* keybits, int tid) {
   const int lg = slot_log2(u.len);
   const int G = kTcRows >> lg;
   const int h0 = u.h0;
@@ -131,9 +131,11 @@ __device__ __forceinline__ void tc_load(const AttnParams& p, const uint8_t* tokm
     cp_async16_tc(sv + off, src + 2 * kHidden, ok ? 16 : 0);
   }
   if (tokmask) {
+    // one bit per key row, a word per warp (row r = thread r)
     const int r = tid;
     const int s = r >> lg, q = r & ((1 << lg) - 1);
-    keyok[r] = (s < nh && q < u.len) ? tokmask[u.start + q] : 0;
+    const uint32_t word = __ballot_sync(0xffffffffu, s < nh && q < u.len && tokmask[u.start + q] != 0);
+    if ((r & 31) == 0) keybits[r >> 5] = word;
   }
 }
 
@@ -202,13 +204,13 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(AttnParams 
   int bi = 0;
   uint32_t ph = 0;
   if (cur.item >= 0) {
-    tc_load(p, tokmask, cur, sm.buf[0], sm.keyok[0], tid);
+    tc_load(p, tokmask, cur, sm.buf[0], sm.keybits[0], tid);
     cp_async_commit_tc();
   }
   while (cur.item >= 0) {
     const TcItem nxt = tc_find(cu, batch, cur.item + gridDim.x, gridDim.x, items);
     if (nxt.item >= 0) {
-      tc_load(p, tokmask, nxt, sm.buf[bi ^ 1], sm.keyok[bi ^ 1], tid);
+      tc_load(p, tokmask, nxt, sm.buf[bi ^ 1], sm.keybits[bi ^ 1], tid);
       cp_async_commit_tc();
       cp_async_wait_tc<1>();
     } else {
@@ -253,17 +255,7 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(AttnParams 
       const int lo = max(off - ch * 32, 0), hi = min(off - ch * 32 + len, 32);
       uint32_t m = 0;
       if (hi > lo) m = (hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u)) & ~((1u << lo) - 1u);
-      if (tokmask) {
-        const uint32_t* kw = reinterpret_cast<const uint32_t*>(sm.keyok[bi] + c_lo + ch * 32);
-        uint32_t km = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint32_t x = kw[i];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) km |= ((x >> (8 * e)) & 0xffu ? 1u : 0u) << (4 * i + e);
-        }
-        m &= km;
-      }
+      if (tokmask) m &= sm.keybits[bi][(c_lo + ch * 32) >> 5];  // chunks start on 32-row words
       return row_ok ? m : 0u;
     };
     float sum = 0.f;
@@ -390,7 +382,7 @@ struct LongSmem {
   uint8_t q[kTcRows * 64];
   uint8_t k[kLongMax * 64];
   uint8_t v[kLongMax * 64];
-  uint8_t keyok[kLongMax];
+  uint32_t keybits[kLongMax / 32];  // bit k: key k usable (padded calls with a token mask)
   float part[2][kTcRows];  // per-half partial row max, then partial row sum
   uint64_t bar_s[2], bar_o, bar_fix;
   uint32_t tmem;
@@ -484,8 +476,11 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
         cp_async16_tc(sk + off, src + kHidden, ok ? 16 : 0);
         cp_async16_tc(sv + off, src + 2 * kHidden, ok ? 16 : 0);
       }
-      if (tokmask)
-        for (int r = tid; r < nkb * kKeyBlk; r += kLongThreads) sm.keyok[r] = r < len ? tokmask[u.start + r] : 0;
+      if (tokmask)  // one bit per key, a word per warp and pass (warp-uniform loop)
+        for (int r = tid; r < nkb * kKeyBlk; r += kLongThreads) {
+          const uint32_t word = __ballot_sync(0xffffffffu, r < len && tokmask[u.start + r] != 0);
+          if ((r & 31) == 0) sm.keybits[r >> 5] = word;
+        }
       cp_async_commit_tc();
       cp_async_wait_tc<0>();
       fence_async_shared();
@@ -524,11 +519,7 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
       {
         const int n_ok = min(max(len - k0, 0), 32);
         uint32_t mm = n_ok >= 32 ? 0xffffffffu : ((1u << n_ok) - 1u);
-        if (tokmask) {
-          uint32_t km = 0;
-          for (int e = 0; e < 32; ++e) km |= (sm.keyok[k0 + e] ? 1u : 0u) << e;
-          mm &= km;
-        }
+        if (tokmask) mm &= sm.keybits[k0 >> 5];
         mk = row_ok ? mm : 0u;
       }
       if (mk != 0xffffffffu) {
