@@ -364,15 +364,18 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(AttnParams 
 //   S_j = Q K_j^T (tcgen05, M = 128, N = 64) into one of two TMEM buffers, so the S-MMA of
 //   block j + 2 is queued behind the P.V-MMA of block j and overlaps the softmax of j + 1;
 //   thread t (query row t) keeps a reference max m and the sum l, and writes
-//   P_j = 2^(s*scale - m*scale) as fp16 pairs over the S columns it read. The reference is
+//   P_j = 2^(s*scale - m*scale) as fp16 pairs into one of two P buffers. The reference is
 //   raised (and l and the row of O in TMEM rescaled) only when a block's max exceeds it by
 //   more than 2^8, so P stays <= 256 and most blocks need no rescale: then the P.V-MMA of
 //   block j is issued without waiting for the one of block j - 1. When some row does need
 //   it, the CTA waits once for the issued MMAs and rescales;
 //   O += P_j V_j (tcgen05, A = P from TMEM, V MN-major in shared memory).
-// Two threads per query row: warps w and w + 4 share TMEM lane quadrant w and take the
-// first and second 32 keys of each block (partial maxima and sums meet in shared memory).
-// TMEM: S buffers at columns [0, 64) and [64, 128), O at [128, 160) (256 allocated);
+// Two threads per query row: warps w and w + 4 share TMEM lane quadrant w; both read the
+// whole 64-key block for its row max (no exchange), then each takes 32 of its keys (the
+// two partial sums meet in shared memory once per item). One CTA barrier per block (before
+// the P.V issue), two when some row raises its reference.
+// TMEM: S buffers at columns [0, 64) and [64, 128), O at [128, 160), P buffers (fp16
+// pairs, 32 columns per block) at [160, 192) and [192, 224) (256 allocated);
 // ~80 KB of shared memory: two CTAs (16 warps) per SM.
 constexpr int kLongThreads = 256;
 constexpr int kLongMax = 512;  // keys per sentence
@@ -445,6 +448,7 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
   tc_fence_after();
   const uint32_t tmem = sm.tmem;
   const uint32_t t_o = tmem + 128;
+  const uint32_t t_p = tmem + 160;  // P of block j in buffer j & 1: never over unread S columns
   const int quad = warp & 3, half = warp >> 2;  // TMEM lane quadrant; key half of a block
   const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
   volatile int* abort_flag = &sm.abort_flag;
@@ -511,28 +515,43 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
       }
       ph_s[b] ^= 1;
       tc_fence_after();
-      float t[32];
-      tmem_ld32(tmem + lane_off + b * kKeyBlk + half * 32, t);
-      // usable keys of this half block: k < len (and the token mask), for a valid query row
-      const int k0 = j * kKeyBlk + half * 32;
-      uint32_t mk;
-      {
+      // usable keys of a 32-key half of this block: k < len (and the token mask), for a
+      // valid query row
+      auto half_mask = [&](int hh) -> uint32_t {
+        const int k0 = j * kKeyBlk + hh * 32;
         const int n_ok = min(max(len - k0, 0), 32);
         uint32_t mm = n_ok >= 32 ? 0xffffffffu : ((1u << n_ok) - 1u);
         if (tokmask) mm &= sm.keybits[k0 >> 5];
-        mk = row_ok ? mm : 0u;
+        return row_ok ? mm : 0u;
+      };
+      // the block's row max: each of the row's two threads reads both halves (no exchange)
+      float bmax;
+      {
+        float t2[32];
+        tmem_ld32(tmem + lane_off + b * kKeyBlk + (half ^ 1) * 32, t2);
+        const uint32_t mk2 = half_mask(half ^ 1);
+        if (mk2 != 0xffffffffu) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) t2[e] = (mk2 >> e) & 1u ? t2[e] : -INFINITY;
+        }
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) mq[(e >> 1) & 3] = fmax3(mq[(e >> 1) & 3], t2[e], t2[e + 1]);
+        bmax = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
       }
+      float t[32];
+      tmem_ld32(tmem + lane_off + b * kKeyBlk + half * 32, t);
+      const uint32_t mk = half_mask(half);
       if (mk != 0xffffffffu) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) t[e] = (mk >> e) & 1u ? t[e] : -INFINITY;
       }
-      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      {
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int e = 0; e < 32; e += 2) mq[(e >> 1) & 3] = fmax3(mq[(e >> 1) & 3], t[e], t[e + 1]);
-      const float pmax = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-      sm.part[half][row] = pmax;
-      __syncthreads();
-      const float bmax = fmaxf(pmax, sm.part[half ^ 1][row]);
+        for (int e = 0; e < 32; e += 2) mq[(e >> 1) & 3] = fmax3(mq[(e >> 1) & 3], t[e], t[e + 1]);
+        bmax = fmaxf(bmax, fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])));
+      }
       // raise the reference max if this block exceeds it by more than 2^8 (always for the
       // first usable block); alpha rescales what was accumulated against the old reference
       float alpha = 1.f;
@@ -541,23 +560,6 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
         alpha = m == -INFINITY ? 0.f : exp2f((m - bmax) * scale);
         l *= alpha;
         m = bmax;
-      }
-      // O holds earlier blocks' P.V (j > 0): rescale its rows once the issued MMAs have landed
-      if (__syncthreads_or(raise && j > 0 && alpha != 1.f)) {
-        if (tid == 0) tc_commit(&sm.bar_fix);  // arrives when every MMA issued so far is done
-        if (!mbar_wait(&sm.bar_fix, ph_fix, abort_flag, nullptr)) {
-          failed = true;
-          break;
-        }
-        ph_fix ^= 1;
-        tc_fence_after();
-        if (half == 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-          float o[32];
-          tmem_ld32(t_o + lane_off, o);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] *= alpha;
-          tmem_st32(t_o + lane_off, o);
-        }
       }
       const float msc = m == -INFINITY ? 0.f : m * scale;
       float bsum = 0.f;
@@ -573,17 +575,36 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
           bsum += e0 + e1;
           w[e >> 1] = pack_half2(e0, e1);
         }
-        tmem_st16(tmem + lane_off + b * kKeyBlk + half * 16, w);  // P pairs over the S columns
+        tmem_st16(t_p + lane_off + b * 32 + half * 16, w);  // P pairs: key k at column k / 2
       }
       l += bsum;  // this half's share of the row sum (both halves use the same reference m)
       tmem_wait_st();
       tc_fence_before();
-      __syncthreads();
+      // one barrier per block: P of every row is written; when some row raised its reference,
+      // O (earlier blocks' P.V) is rescaled first, once the issued MMAs have landed
+      if (__syncthreads_or(raise && j > 0 && alpha != 1.f)) {
+        if (tid == 0) tc_commit(&sm.bar_fix);  // arrives when every MMA issued so far is done
+        if (!mbar_wait(&sm.bar_fix, ph_fix, abort_flag, nullptr)) {
+          failed = true;
+          break;
+        }
+        ph_fix ^= 1;
+        tc_fence_after();
+        if (half == 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          float o[32];
+          tmem_ld32(t_o + lane_off, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] *= alpha;
+          tmem_st32(t_o + lane_off, o);
+        }
+        tc_fence_before();
+        __syncthreads();
+      }
       if (tid == 0) {
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < kKeyBlk / 16; ++k)
-          tc_mma_f16_ts(t_o, tmem + b * kKeyBlk + k * 8,
+          tc_mma_f16_ts(t_o, t_p + b * 32 + k * 8,
                         sw64_mnmajor_desc(smem_u32(sm.v) + (j * (kKeyBlk / 16) + k) * 1024), idesc_o,
                         (j > 0 || k > 0) ? 1u : 0u);
         if (j + 1 == nkb) tc_commit(&sm.bar_o);  // the item's last P.V
