@@ -147,6 +147,20 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&w)[16
       "r"(w[10]), "r"(w[11]), "r"(w[12]), "r"(w[13]), "r"(w[14]), "r"(w[15])
       : "memory");
 }
+// 32 lanes x 16 columns -> 16 registers per thread
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tmem_st8_zero(uint32_t taddr) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(0)
                : "memory");
@@ -455,7 +469,7 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
   constexpr uint32_t idesc_s = idesc_f16_f32(128, kKeyBlk);            // Q K^T, both K-major
   constexpr uint32_t idesc_o = idesc_f16_f32(128, 32) | (1u << 16);    // P V, V MN-major
   const float scale = p.scale_log2;
-  uint32_t ph_s[2] = {0, 0}, ph_o = 0, ph_fix = 0;
+  uint32_t ph_s = 0, ph_o = 0, ph_fix = 0;  // ph_s bit b: phase of bar_s[b]
   constexpr float kRescaleLog2 = 8.f;  // raise the reference max when a block exceeds it by 2^8
 
   for (LongItem u = long_find(cu, batch, blockIdx.x, gridDim.x, items, p.min_len); u.item >= 0;
@@ -509,11 +523,11 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
     bool failed = false;
     for (int j = 0; j < nkb; ++j) {
       const int b = j & 1;
-      if (!mbar_wait(&sm.bar_s[b], ph_s[b], abort_flag, nullptr)) {
+      if (!mbar_wait(&sm.bar_s[b], (ph_s >> b) & 1u, abort_flag, nullptr)) {
         failed = true;
         break;
       }
-      ph_s[b] ^= 1;
+      ph_s ^= 1u << b;
       tc_fence_after();
       // usable keys of a 32-key half of this block: k < len (and the token mask), for a
       // valid query row
@@ -619,8 +633,8 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
     ph_o ^= 1;
     tc_fence_after();
     {
-      float o[32];
-      tmem_ld32(t_o + lane_off, o);
+      float o[16];  // this half's 16 of the row's 32 output dimensions
+      tmem_ld16(t_o + lane_off + half * 16, o);
       if (row_ok) {
         const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
         __half* out = p.ctx + static_cast<size_t>(u.start + q0 + row) * kHidden + u.h * kHeadDim + half * 16;
@@ -629,8 +643,7 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
           uint4 wv;
           uint32_t* ww = reinterpret_cast<uint32_t*>(&wv);
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            ww[e] = pack_half2(o[half * 16 + j * 8 + 2 * e] * inv, o[half * 16 + j * 8 + 2 * e + 1] * inv);
+          for (int e = 0; e < 4; ++e) ww[e] = pack_half2(o[j * 8 + 2 * e] * inv, o[j * 8 + 2 * e + 1] * inv);
           *reinterpret_cast<uint4*>(out + j * 8) = wv;
         }
       }
