@@ -579,13 +579,12 @@ __global__ void __launch_bounds__(kLongThreads, 2) attention_long_kernel(AttnPar
       float bsum = 0.f;
       {
         uint32_t w[16];
+        // masked keys already hold -inf, so 2^(-inf) = 0 there: no per-key select
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           float e0, e1;
           asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(fmaf(t[e], scale, -msc)));
           asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(fmaf(t[e + 1], scale, -msc)));
-          e0 = (mk >> e) & 1u ? e0 : 0.f;
-          e1 = (mk >> (e + 1)) & 1u ? e1 : 0.f;
           bsum += e0 + e1;
           w[e >> 1] = pack_half2(e0, e1);
         }
