@@ -24,6 +24,8 @@
 #include "common.cuh"
 #include "internal.h"
 
+#include <type_traits>
+
 namespace bbh {
 
 constexpr int kTcThreads = 128;
@@ -273,7 +275,63 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(AttnParams 
       return row_ok ? m : 0u;
     };
     float sum = 0.f;
-    if (warp_active) {
+    // One or two 32-key chunks (sentences of <= 64 tokens): the row's scores stay in
+    // registers between the max and the exponentials (one TMEM read), masked scores are
+    // set to -inf so that their 2^(...) is 0 without a second select.
+    auto short_row = [&](auto nc_tag) {
+      constexpr int NC = decltype(nc_tag)::value;
+      const uint32_t trow = tmem + lane_off;
+      float t[NC][32];
+      uint32_t m[NC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) m[c] = chunk_mask(c);
+      if constexpr (NC == 1) {
+        tmem_ld32(trow + c_lo, t[0]);
+      } else {
+        float t64[64];
+        tmem_ld64(trow + c_lo, trow + c_lo + 32, t64);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) t[0][j] = t64[j], t[1][j] = t64[32 + j];
+      }
+      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        if (m[c] != 0xffffffffu) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) t[c][j] = (m[c] >> j) & 1u ? t[c][j] : -INFINITY;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) mq[(j >> 1) & 3] = fmax3(mq[(j >> 1) & 3], t[c][j], t[c][j + 1]);
+      }
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      const float msc = mx == -INFINITY ? 0.f : mx * scale;
+      float sq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        uint32_t w[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float e0, e1;
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(fmaf(t[c][j], scale, -msc)));
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(fmaf(t[c][j + 1], scale, -msc)));
+          sq[j & 3] += e0;
+          sq[(j + 1) & 3] += e1;
+          w[j >> 1] = pack_half2(e0, e1);
+        }
+        tmem_st16(trow + (c_lo >> 1) + c * 16, w);
+      }
+      sum = (sq[0] + sq[1]) + (sq[2] + sq[3]);
+      const int z_lo = c_lo >> 4, z_hi = z_lo + NC * 2, z_used = kused >> 4;
+#pragma unroll 1
+      for (int z = 0; z < z_used; ++z)
+        if (z < z_lo || z >= z_hi) tmem_st8_zero(trow + z * 8);
+      tmem_wait_st();
+    };
+    if (warp_active && nchunk == 1) {
+      short_row(std::integral_constant<int, 1>{});
+    } else if (warp_active && nchunk == 2) {
+      short_row(std::integral_constant<int, 2>{});
+    } else if (warp_active) {
       const uint32_t trow = tmem + lane_off;
       // pass 1: row max of the raw scores over this row's usable keys
       float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
