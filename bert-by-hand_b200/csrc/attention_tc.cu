@@ -332,9 +332,15 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(AttnParams 
     } else if (warp_active && nchunk == 2) {
       short_row(std::integral_constant<int, 2>{});
     } else if (warp_active) {
+      // Three or four chunks: one pass with a lazily raised reference (as in the long
+      // kernel): the first chunk's max is the reference m; a later chunk whose max exceeds
+      // it by more than 2^8 raises it and rescales the P already written (this row's own
+      // TMEM lane) and the partial sums, so P stays <= 256 in fp16. P of chunk ch goes to
+      // columns 16 ch .. +16, over S columns already read.
       const uint32_t trow = tmem + lane_off;
-      // pass 1: row max of the raw scores over this row's usable keys
-      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      constexpr float kRaise = 8.f;
+      float mref = -INFINITY;
+      float sq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
       for (int ch = 0; ch < nchunk; ++ch) {
         const uint32_t m = chunk_mask(ch);
@@ -344,35 +350,47 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(AttnParams 
 #pragma unroll
           for (int j = 0; j < 32; ++j) t[j] = (m >> j) & 1u ? t[j] : -INFINITY;
         }
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int j = 0; j < 32; j += 2) mq[(j >> 1) & 3] = fmax3(mq[(j >> 1) & 3], t[j], t[j + 1]);
-      }
-      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-      const float msc = mx == -INFINITY ? 0.f : mx * scale;
-      // pass 2: p = 2^(s * scale - max * scale), row sum; P (fp16 pairs) overwrites the S
-      // columns already read: keys [32 ch, 32 ch + 32) of the range -> columns 16 ch .. +16
-      float sq[4] = {0.f, 0.f, 0.f, 0.f};
+        const float cmax = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+        float alpha = 1.f;
+        if (cmax != -INFINITY && (mref == -INFINITY || (cmax - mref) * scale > kRaise)) {
+          if (mref != -INFINITY) {
+            alpha = exp2f((mref - cmax) * scale);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) sq[k] *= alpha;
+          }
+          mref = cmax;
+        }
+        // TMEM loads and stores are warp-collective: the whole warp rewrites its earlier P
+        // when any of its rows raised (alpha 1 leaves a row unchanged)
+        if (ch > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          tmem_wait_st();  // this warp's earlier P stores, read back below
 #pragma unroll 1
-      for (int ch = 0; ch < nchunk; ++ch) {
-        const uint32_t m = chunk_mask(ch);
-        float t[32];
-        tmem_ld32(trow + c_lo + ch * 32, t);
+          for (int c = 0; c < ch; ++c) {
+            float pv[16];
+            tmem_ld16(trow + (c_lo >> 1) + c * 16, pv);
+            uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float e;
-          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(fmaf(t[j], scale, -msc)));
-          t[j] = e;
+            for (int i = 0; i < 16; ++i) {  // fp32 alpha, one rounding back to fp16
+              const uint32_t u = __float_as_uint(pv[i]);
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u));
+              w[i] = pack_half2(f.x * alpha, f.y * alpha);
+            }
+            tmem_st16(trow + (c_lo >> 1) + c * 16, w);
+          }
         }
-        if (m != 0xffffffffu) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) t[j] = (m >> j) & 1u ? t[j] : 0.f;
-        }
+        const float msc = mref == -INFINITY ? 0.f : mref * scale;
         uint32_t w[16];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
-          sq[j & 3] += t[j];
-          sq[(j + 1) & 3] += t[j + 1];
-          w[j >> 1] = pack_half2(t[j], t[j + 1]);
+          float e0, e1;
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(fmaf(t[j], scale, -msc)));
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(fmaf(t[j + 1], scale, -msc)));
+          sq[j & 3] += e0;
+          sq[(j + 1) & 3] += e1;
+          w[j >> 1] = pack_half2(e0, e1);
         }
         tmem_st16(trow + (c_lo >> 1) + ch * 16, w);
       }
