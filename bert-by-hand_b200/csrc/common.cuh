@@ -443,26 +443,27 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // erf-GELU, x * Phi(x) = x / 2 * (1 + tanh(y(x))), where y(x) = atanh(erf(x / sqrt 2))
-// is approximated by an odd degree-9 polynomial on [-5.5, 5.5] (x clamped there); the
+// is approximated by an odd degree-9 polynomial fitted on [-5.5, 5.5]; the
 // coefficients are this project's own weighted least-squares fit,
 //   y(x) ~ x (0.797853484 + 3.64356497e-2 x^2 - 1.12335663e-4 x^4 - 3.22934132e-5 x^6
 //             + 1.19315286e-6 x^8).
 // It is evaluated on a pair of fp16 values (the GEMM output rounded to fp16, as the
 // reference's separate GELU pass sees it) in packed half2 arithmetic: the polynomial runs
 // in u = x^2 / 16 so that its fp16 coefficients stay normal and well scaled, and one
-// hardware tanh.approx.f16x2 serves both elements. Max abs error vs exact GELU ~1.5e-3
+// hardware tanh.approx.f16x2 serves both elements. Outside the fit range no clamp is
+// needed: y(x) / x = p(x^2) >= 0.798 for every x (the polynomial in x^2 has no root), so for
+// |x| >= 5.5 |y| >= 10.4 and tanh is +-1 in fp16 (y overflowing to +-inf included), which
+// gives x or 0 as GELU does. Max abs error vs exact GELU ~1.5e-3
 // (under one fp16 ulp of the output); tests/test_gpu_kernels.py checks it against torch's
 // erf GELU and the reference's GELU golden vectors.
 __device__ __forceinline__ uint32_t gelu_half2(uint32_t xw) {
   const __half2 x = *reinterpret_cast<const __half2*>(&xw);
-  const __half2 lim = __float2half2_rn(5.5f);
-  const __half2 xc = __hmin2(__hmax2(x, __hneg2(lim)), lim);
-  const __half2 u = __hmul2(__hmul2(xc, xc), __float2half2_rn(0.0625f));
+  const __half2 u = __hmul2(__hmul2(x, x), __float2half2_rn(0.0625f));
   __half2 z = __hfma2(__float2half2_rn(1.19315286e-06f * 65536.f), u, __float2half2_rn(-3.22934132e-05f * 4096.f));
   z = __hfma2(z, u, __float2half2_rn(-1.12335663e-04f * 256.f));
   z = __hfma2(z, u, __float2half2_rn(3.64356497e-02f * 16.f));
   z = __hfma2(z, u, __float2half2_rn(7.97853484e-01f));
-  z = __hmul2(z, xc);
+  z = __hmul2(z, x);
   uint32_t zw = *reinterpret_cast<uint32_t*>(&z), tw;
   asm("tanh.approx.f16x2 %0, %1;" : "=r"(tw) : "r"(zw));
   const __half2 t = *reinterpret_cast<const __half2*>(&tw);
