@@ -9,18 +9,22 @@
 //      swizzled rows of 32 fp16; rows past the sentence are zero-filled), double buffered
 //      across tiles.
 //   2. One thread issues S = Q K^T (tcgen05.mma, M = N = 128, K = 32) into TMEM.
-//   3. Thread t owns query row t (TMEM lane t). Pass 1 reads the columns of its slot's keys
-//      and takes the row max (a key of another head, or past the sentence end, is dropped);
-//      pass 2 exponentiates in the exp2 domain, sums, and writes P as fp16 pairs back into
-//      the TMEM columns it has just read (P[k] at column k/2) -- no warp shuffles, no
-//      shared-memory or global copy of S or P. Warps whose 32 rows hold no query skip.
+//   3. Thread t owns query row t (TMEM lane t) and reads the columns of its slot's keys (a
+//      key of another head, or past the sentence end, is dropped). Rows of up to 64 keys
+//      keep their scores in registers: row max, then exp2-domain exponentials and sum;
+//      longer rows walk 32-key chunks once against a reference max raised (with a
+//      warp-wide rewrite of the P already written) only when a chunk exceeds it by more
+//      than 2^8. P goes as fp16 pairs back into TMEM columns already read (P[k] at column
+//      k/2) -- no warp shuffles, no shared-memory or global copy of S or P. Warps whose 32
+//      rows hold no query skip.
 //   4. One thread issues O = P V (tcgen05.mma with A = P read from TMEM, M = 128, N = 32,
 //      K = the keys in use, V as an MN-major shared-memory operand) into columns 64-95;
 //      thread t normalises its row by its softmax sum and stores the 32 head dimensions to
 //      the merged context [T, 384].
 // TMEM 128 columns, 48 KB shared memory and 128 registers per thread: four CTAs per SM.
-// A key is also dropped where the token mask is 0 (padded calls), as softmax.cu:43-59 does;
-// a row with no usable key gives zeros.
+// A key is also dropped where the token mask is 0 (padded calls), as softmax.cu:43-59 does
+// (one bit per key row, built with __ballot_sync when the tile is staged); a row with no
+// usable key gives zeros.
 #include "common.cuh"
 #include "internal.h"
 
