@@ -173,12 +173,35 @@ __global__ void __launch_bounds__(kRowThreads) pool_l2_kernel(PoolParams p) {
 #pragma unroll
     for (int i = 0; i < 12; ++i) acc[i] = 0.f;
     int n = 0;
-    for (int t = start + warp; t < end; t += kRowThreads / 32) {
-      if (!p.tokmask || p.tokmask[t]) {
-        float f[12];
-        load_row12(p.hidden + static_cast<size_t>(t) * kHidden, lane, f);
+    // each warp takes rows warp, warp + W, ... (W warps), four at a time so that their
+    // loads are in flight together (the sentence's rows are independent until summed)
+    constexpr int W = kRowThreads / 32;
+    for (int t0 = start + warp; t0 < end; t0 += 4 * W) {
+      uint2 u[4][3];
+      bool use[4];
 #pragma unroll
-        for (int i = 0; i < 12; ++i) acc[i] += f[i];
+      for (int r = 0; r < 4; ++r) {
+        const int t = t0 + r * W;
+        use[r] = t < end && (!p.tokmask || p.tokmask[t]);
+        if (use[r]) {
+          const __half* row = p.hidden + static_cast<size_t>(t) * kHidden;
+#pragma unroll
+          for (int i = 0; i < 3; ++i) u[r][i] = __ldg(reinterpret_cast<const uint2*>(row + i * 128 + lane * 4));
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        if (!use[r]) continue;
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+          const __half2* hh = reinterpret_cast<const __half2*>(&u[r][i]);
+          const float2 a = __half22float2(hh[0]);
+          const float2 b = __half22float2(hh[1]);
+          acc[i * 4 + 0] += a.x;
+          acc[i * 4 + 1] += a.y;
+          acc[i * 4 + 2] += b.x;
+          acc[i * 4 + 3] += b.y;
+        }
         ++n;
       }
     }
