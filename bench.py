@@ -1,14 +1,17 @@
 """Throughput benchmark: MiniLM-L6 sentence embeddings (sentences/s) on 1..8 B200s.
 
 Default workload (configs[3] of the task's baseline): sentences with lengths uniform in
-[8, 128] tokens, length-sorted into batches of 1024, packed with cu_seqlens (no padding),
-131,072 sentences per GPU per step (so 8 GPUs together process the 1,048,576-sentence
-corpus each step); one weight replica per GPU, no inter-GPU traffic in the forward, and
-the fp16 [n, 384] embeddings all-gathered over NCCL at the end of each step when N > 1.
+[8, 128] tokens, 131,072 sentences per GPU per step, so N GPUs embed one corpus of
+N x 131,072 sentences each step (the 1,048,576-sentence corpus at N = 8; weak scaling).
+Every rank plans the same corpus with bbh_plan_batches(..., world = N): length-sorted
+batches of 1024 sentences, packed with cu_seqlens (no padding), assigned to ranks by
+longest-processing-time on their FLOPs. One weight replica per GPU, no inter-GPU traffic in
+the forward; the fp16 [n, 384] embeddings are gathered to rank 0 in corpus order (one NCCL
+gather over NVLink plus an index copy on rank 0) at the end of every step.
 
-A step = one pass of bert_embed over the rank's whole shard. Timing: W untimed warm-up
-steps, then K steps between a barrier + cuda synchronize, CUDA events on the launch
-stream, max over ranks. One JSON line from rank 0.
+A step = every rank embeds its batches + the gather. Timing: W untimed warm-up steps, then
+K steps between a barrier + cuda synchronize, CUDA events on the launch stream, max over
+ranks. One JSON line from rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg3|cfg2|cfg1|cfg0|cfg4]
     python bench.py --impl reference ...   # CPU reference arm (torch fp32 forward, host cores)
@@ -19,12 +22,13 @@ stand in for the pretrained checkpoint and the STS corpus (no network here).
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
-import math
 import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -44,12 +48,18 @@ WORKLOADS = {
     "cfg0": ("MiniLM-L6, batch 64 x 9 real tokens padded to seq 16", 6, False, ("fixed", 9, 16), 16384, 64),
     "cfg4": ("MiniLM-L12, batch 32 x 512 real tokens", 12, False, ("fixed", 512, 512), 1024, 32),
 }
+# the other workloads' short runs added to the default line (device-resident + e2e)
+SIDE_RUNS = {"cfg2": 131072, "cfg1": 16384, "cfg4": 1024}
 
 # GEMM shapes per token and layer, by kernel kind: (N, K)
 GEMM_NK = {"qkv_gemm": (1152, 384), "o_gemm_ln": (384, 384), "ffn1_gemm_gelu": (1536, 384),
-           "ffn2_gemm_ln": (384, 1536), "ffn_fused": (1536, 2 * 384)}  # fused: both FFN GEMMs
-# algorithmic HBM bytes per token for the memory-bound kernels
-MEM_BYTES = {"embed_ln": 8 + 768 + 768, "pool_l2": 768, "attention": 4 * 768}
+           "ffn2_gemm_ln": (384, 1536)}
+# algorithmic HBM bytes per token (per layer for the layer kernels): activations read and
+# written once; the GEMMs' weights (N x K fp16) are added once per launch
+ALGO_BYTES = {"embed_ln": 8 + 768 + 768, "pool_l2": 768, "attention": 4 * 768,
+              "qkv_gemm": 768 + 2304, "o_gemm_ln": 768 + 768 + 768, "ffn1_gemm_gelu": 768 + 3072,
+              "ffn2_gemm_ln": 3072 + 768 + 768}
+PER_LAYER = {"qkv_gemm", "attention", "o_gemm_ln", "ffn1_gemm_gelu", "ffn2_gemm_ln"}
 
 
 def env_int(name, default):
@@ -85,6 +95,43 @@ def profiled_traffic():
             return json.load(f)
     except Exception:
         return {}
+
+
+def traffic_per_launch(kind, bytes_per_token, tokens_per_pass, layers, launches):
+    """DRAM bytes of ONE launch: ncu's bytes per token x the tokens one launch processes
+    (a pass over the workload runs `launches` launches of this kind, one per layer of each
+    forward for the layer kernels)."""
+    toks = tokens_per_pass * (layers if kind in PER_LAYER else 1)
+    return bytes_per_token * toks / launches
+
+
+def kernel_entry(kind, ms_total, launches, tokens, layers, attn_flops, peaks):
+    """Per-kernel figures for one timed pass: `tokens` = rows processed by one pass over the
+    workload (per layer for the layer kernels). Achieved FLOP/s and algorithmic bytes/s,
+    each against its measured peak, and the kernel's roofline (the larger of its
+    tensor-core time and its HBM time at the measured peaks) as a fraction of its time."""
+    hbm, _, tf_sust = peaks
+    t = ms_total / 1000.0
+    rows = tokens * (layers if kind in PER_LAYER else 1)
+    e = {"ms_total": round(ms_total, 3), "launches": int(launches), "us_per_launch": round(1000 * ms_total / launches, 2)}
+    flops = 0.0
+    nbytes = ALGO_BYTES[kind] * rows
+    if kind in GEMM_NK:
+        N, K = GEMM_NK[kind]
+        flops = 2.0 * rows * N * K
+        nbytes += 2.0 * N * K * launches
+    elif kind == "attention":
+        flops = attn_flops
+    t_tensor = flops / (tf_sust * 1e12)
+    t_hbm = nbytes / (hbm * 1e9)
+    if flops:
+        e["tflops"] = round(flops / t / 1e12, 1)
+        e["tensor_frac"] = round(t_tensor / t, 3)
+    e["gbs"] = round(nbytes / t / 1e9, 1)
+    e["hbm_frac"] = round(t_hbm / t, 3)
+    e["bound"] = "tensor" if t_tensor > t_hbm else "hbm"
+    e["roofline_frac"] = round(max(t_tensor, t_hbm) / t, 3)
+    return e
 
 
 class ClockSampler:
@@ -176,9 +223,65 @@ def cpu_forward_rate(workload: str, budget_s: float, seed: int = 99, warm: bool 
     return done / dt, torch.get_num_threads(), f"{done} sentences in batches of {B} ({dt:.1f} s, torch fp32 CPU oracle)"
 
 
+def reference_cuda_times():
+    """The reference's own CUDA (its unmodified sources built into oracle/_ref/libbbh_ref.so
+    for sm_100a) timed on this GPU with CUDA events, device-resident inputs, on the same
+    synthetic weights: bench/bench.cu's repeated bert_embed at configs[0] (64 x 9 tokens
+    padded to 16) and configs[1] (padded to 128), and bench/corpus.cu's dynamic-length loop
+    (length-sorted batches of 64, each padded to its longest rounded to 16) over configs[2]
+    (2000 sentences) and a 65,536-sentence sample of configs[3] (lengths U[8,128])."""
+    lib_path = os.path.join(ROOT, "oracle", "_ref", "libbbh_ref.so")
+    if not os.path.exists(lib_path):
+        return {"unavailable": "oracle/_ref/libbbh_ref.so was not built (needs the reference sources at build time)"}
+    try:
+        import torch
+
+        if not torch.cuda.is_available():
+            return {"unavailable": "no GPU on this host"}
+        from oracle import model as om
+
+        L = ctypes.CDLL(lib_path)
+        root = tempfile.mkdtemp(prefix="bbh_refw_")
+        om.save_weights(om.make_weights(0), os.path.join(root, "weights"))
+        p = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+        out = {"source": "reference CUDA kernels (wmma, fp16 accumulate) built for sm_100a, CUDA events, "
+                         "device-resident inputs; same seeded random-init weights"}
+        for name, (B, real, S, iters) in {"cfg0": (64, 9, 16, 300), "cfg1": (64, 9, 128, 100)}.items():
+            ids, types, mask = om.padded_batch(B, real, S, seed=1)
+            keep = [np.ascontiguousarray(a, np.int32) for a in (ids, types, mask)]
+            emb = np.zeros((B, 384), np.float16)
+            ms = ctypes.c_float(0)
+            rc = L.ref_embed(root.encode(), *(p(a) for a in keep), p(emb), B, S, iters, ctypes.byref(ms))
+            if rc != 0:
+                out[name] = {"unavailable": f"ref_embed returned {rc}"}
+                continue
+            out[name] = {"ms_per_forward": round(ms.value, 4), "sentences_per_s": round(B / (ms.value / 1e3), 1),
+                         "batch": B, "seq": S}
+        for name, (lens, iters) in {
+                "cfg2": (om.lognormal_lengths(2000, seed=2)[0], 20),
+                "cfg3_sample": (om.uniform_lengths(65536, seed=3)[0], 2)}.items():
+            import synthetic as sy
+
+            ids = sy.sentence_tokens(lens.astype(np.int32), 5)
+            cu = np.zeros(lens.size + 1, np.int32)
+            cu[1:] = np.cumsum(lens)
+            ms = ctypes.c_float(0)
+            rc = L.ref_corpus(root.encode(), p(ids), p(cu), int(lens.size), 64, iters, ctypes.byref(ms), None)
+            if rc != 0:
+                out[name] = {"unavailable": f"ref_corpus returned {rc}"}
+                continue
+            out[name] = {"ms_per_pass": round(ms.value, 3), "sentences": int(lens.size),
+                         "sentences_per_s": round(lens.size / (ms.value / 1e3), 1),
+                         "loop": "bench/corpus.cu dynamic: length-sorted batches of 64 padded to ceil16(max)"}
+        return out
+    except Exception as e:  # the reference arm still prints its CPU line
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+
+
 def run_reference(args):
     """--impl reference: the reference path's CPU implementation (oracle port) timed on the
-    host cores, rank 0 only; K steps, each a bounded sample of the workload."""
+    host cores, rank 0 only; K steps, each a bounded sample of the workload. The reference's
+    own CUDA kernels, timed on this GPU, are reported beside it (`reference_cuda`)."""
     rank = env_int("RANK", 0)
     if rank != 0:
         return
@@ -201,7 +304,234 @@ def run_reference(args):
                          "sample": f"per step: {sample}"},
         "e2e": {"value": round(value, 2), "unit": "sentences/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_reference_cuda:
+        line["reference_cuda"] = reference_cuda_times()
     print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------------------
+class Ctx:
+    def __init__(self, rank, world, local, dev, args):
+        self.rank, self.world, self.local, self.dev, self.args = rank, world, local, dev, args
+
+
+def measure(ctx, workload, n_per_gpu, steps, warmup, e2e_steps, gather=True, clocks=None, kernel_pass=True):
+    """Device-resident timing, end-to-end timing and a per-kernel pass of one workload.
+    Returns a dict (rank 0's view; timings are max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    import bbh
+    import sharding
+    import synthetic as sy
+
+    rank, world, dev, args = ctx.rank, ctx.world, ctx.dev, ctx.args
+    desc, layers, packed, spec, _, batch = WORKLOADS[workload]
+    gw = bbh.ModelWeights.from_numpy(sy.random_weights(0, layers), layers, ctx.local)
+    stream = torch.cuda.current_stream(dev)
+    lane_streams = [stream] + [torch.cuda.Stream(dev) for _ in range(args.lanes - 1)]
+    i32 = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.int32, device=dev)
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    n_global = n_per_gpu * world
+    if packed:
+        # one corpus, the same on every rank; the plan splits it
+        lengths = make_lengths(spec, n_global, seed=3)
+        ids = sy.sentence_tokens(lengths, 3)
+        types = np.zeros_like(ids)
+        offsets = np.zeros(n_global + 1, np.int64)
+        offsets[1:] = np.cumsum(lengths)
+        max_len = int(lengths.max())
+        plan = bbh.plan_batches(lengths, batch, batch * max_len, world)
+        sh = sharding.shard(plan, rank, ids, types, offsets)
+        max_tokens = sh.max_tokens
+        m_rank = int(sh.order.size)
+        d_ids, d_types = i32(sh.ids), i32(sh.types)
+        d_cu = [i32(b.cu) for b in sh.batches]
+        tok_per_pass = int(sh.ids.size)
+        attn_flops = 4.0 * 384 * float((lengths[sh.order].astype(np.float64) ** 2).sum()) * layers
+        mean_len = float(lengths.mean())
+    else:
+        S, Lr = spec[2], spec[1]
+        m_rank = n_per_gpu
+        pid = np.zeros((m_rank, S), np.int32)
+        pid[:, :Lr] = sy.sentence_tokens(np.full(m_rank, Lr, np.int32), 3 + rank).reshape(m_rank, Lr)
+        pmask = np.zeros((m_rank, S), np.int32)
+        pmask[:, :Lr] = 1
+        d_ids, d_types, d_mask = i32(pid), i32(np.zeros_like(pid)), i32(pmask)
+        max_tokens, max_len = batch * S, S
+        tok_per_pass = m_rank * S
+        attn_flops = 4.0 * 384 * S * S * m_rank * layers
+        mean_len = float(Lr)
+        plan = None
+    ws = bbh.Workspace(gw, max_tokens, batch, max_len)
+    lanes = [ws] + [bbh.Workspace(gw, max_tokens, batch, max_len) for _ in range(args.lanes - 1)]
+    ws.set_corpus_lanes(args.lanes)
+
+    gathered = None
+    if packed:
+        gat = sharding.Rank0Gather(plan, world, rank, n_global, dev) if gather else None
+        emb = gat.send if gat is not None else torch.empty((max(m_rank, 1), 384), dtype=torch.float16, device=dev)
+        n_forwards = len(sh.batches)
+    else:
+        emb = torch.empty((m_rank, 384), dtype=torch.float16, device=dev)
+        gat = None
+        n_forwards = (m_rank + batch - 1) // batch
+        gathered = ([torch.empty_like(emb) for _ in range(world)] if rank == 0 else None) if (gather and world > 1) else None
+
+    def forward_all(nlanes=None):
+        nl = nlanes or len(lanes)
+        for ls in lane_streams[1:nl]:
+            ls.wait_stream(stream)
+        if packed:
+            for bi, b in enumerate(sh.batches):
+                lw, lst = lanes[bi % nl], lane_streams[bi % nl]
+                lw.embed_varlen(d_ids[b.tok:b.tok + b.tokens], d_types[b.tok:b.tok + b.tokens], d_cu[bi], b.max_len,
+                                out=emb[b.row:b.row + b.count], stream=lst)
+        else:
+            for bi, first in enumerate(range(0, m_rank, batch)):
+                c = min(batch, m_rank - first)
+                lw, lst = lanes[bi % nl], lane_streams[bi % nl]
+                lw.embed(d_ids[first:first + c], d_types[first:first + c], d_mask[first:first + c],
+                         out=emb[first:first + c], stream=lst)
+        for ls in lane_streams[1:nl]:
+            stream.wait_stream(ls)
+
+    def step():
+        forward_all()
+        if gat is not None:
+            gat(emb)
+        elif gather and world > 1:
+            dist.gather(emb, gathered, dst=0)
+
+    # ---------------- device-resident timed region ----------------
+    for _ in range(warmup):
+        step()
+    if ws.device_error() != 0:
+        raise RuntimeError("device flagged an input error")
+    sync_all()
+    if clocks:
+        clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    sync_all()
+    clock_info = clocks.stop() if clocks else None
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    value = n_global * steps / (ms / 1000.0)
+    res = {"workload": workload, "desc": desc, "layers": layers, "packed": packed, "batch": batch,
+           "n_per_gpu": n_per_gpu, "n_global": n_global, "value": value, "ms": ms, "steps": steps,
+           "clocks": clock_info, "launches": steps * n_forwards * ws.launches_per_forward,
+           "tok_per_pass": tok_per_pass, "mean_len": mean_len, "m_rank": m_rank}
+
+    # ---------------- end to end through the public API, host buffers ----------------
+    if e2e_steps > 0:
+        h2d = d2h = 0
+        if packed and world == 1:
+            # bbh_embed_corpus over the host corpus: pinned double-buffered staging, H2D of
+            # ids/types/cu_seqlens, one graph replay per batch, D2H to corpus order
+            h_emb = np.zeros((n_global, 384), np.float16)
+
+            def e2e_step():
+                ws.embed_corpus(ids, types, offsets, plan, rank=0, out=h_emb)
+
+            h2d = 8 * int(lengths.sum()) + 4 * (n_global + plan.n_batches)
+            d2h = 768 * n_global
+            note = ("bbh_embed_corpus: host corpus -> pinned double-buffered staging -> H2D -> forward -> D2H to "
+                    "corpus order, host-timed around the call")
+        elif packed:
+            # every rank: bbh_embed_corpus_device (host ids in, embeddings left on the
+            # device), the NCCL gather to rank 0 in corpus order, one D2H there
+            h_out = torch.empty((n_global, 384), dtype=torch.float16, pin_memory=True) if rank == 0 else None
+
+            def e2e_step():
+                ws.embed_corpus_device(ids, types, offsets, plan, rank=rank, out=gat.send)
+                g = gat(gat.send)
+                if rank == 0:
+                    h_out.copy_(g, non_blocking=True)
+                    torch.cuda.current_stream(dev).synchronize()
+
+            h2d = 8 * int(lengths.sum()) + 4 * (n_global + plan.n_batches)  # whole job, all ranks
+            d2h = 768 * n_global  # rank 0
+            note = ("per rank bbh_embed_corpus_device (host corpus -> pinned staging -> H2D -> forward, embeddings "
+                    "left on the device), NCCL gather to rank 0 + index copy to corpus order, D2H on rank 0; "
+                    "host-timed, max over ranks; bytes are whole-job totals")
+        else:
+            h_emb = np.zeros((m_rank, 384), np.float16)
+            host_ids, host_mask = np.ascontiguousarray(pid), np.ascontiguousarray(pmask)
+            host_types = np.zeros_like(host_ids)
+
+            def e2e_step():
+                ws.embed_padded(host_ids, host_types, host_mask, batch, out=h_emb)
+
+            h2d = 12 * m_rank * spec[2] * world
+            d2h = 768 * m_rank * world
+            note = ("bbh_embed_padded per rank: host ids/types/mask -> pinned double-buffered staging -> H2D -> "
+                    "bert_embed per batch -> D2H, host-timed around the call, max over ranks")
+        e2e_step()
+        sync_all()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            e2e_step()
+        sync_all()
+        e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0) / e2e_steps
+        res["e2e"] = {"value": round(n_global / (e2e_ms / 1000.0), 1), "unit": "sentences/s",
+                      "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": e2e_steps,
+                      "note": note}
+
+    # ---------------- per-kernel timing pass (same workload, eager, CUDA events) ----------------
+    if kernel_pass:
+        ws.set_kernel_timing(True)
+        forward_all(nlanes=1)
+        kt = ws.kernel_times()
+        ws.set_kernel_timing(False)
+        hbm, tf_burst, tf_sust, peak_src = measured_peaks()
+        per_kernel = {}
+        for k, (kms, cnt) in kt.items():
+            if cnt:
+                per_kernel[k] = kernel_entry(k, kms, cnt, tok_per_pass, layers, attn_flops, (hbm, tf_burst, tf_sust))
+        total_k = sum(v["ms_total"] for v in per_kernel.values())
+        for v in per_kernel.values():
+            v["share"] = round(v["ms_total"] / total_k, 3)
+        res["kernels"] = per_kernel
+        res["peaks"] = {"hbm_gbs": hbm, "bf16_tflops_sustained": tf_sust, "source": peak_src}
+    sync_all()
+    return res
+
+
+def roofline_of(res, layers):
+    """The line's roofline object for the dominant kernel of the per-kernel pass."""
+    per_kernel = res["kernels"]
+    dom = max(per_kernel, key=lambda k: per_kernel[k]["ms_total"])
+    dk = per_kernel[dom]
+    hbm, tf_sust = res["peaks"]["hbm_gbs"], res["peaks"]["bf16_tflops_sustained"]
+    tr = profiled_traffic().get(dom)
+    traffic_b = (round(traffic_per_launch(dom, tr["bytes_per_token"], res["tok_per_pass"], layers, dk["launches"]))
+                 if tr else None)
+    if dk["bound"] == "tensor":
+        achieved, peak, unit = dk["tflops"], tf_sust, "TFLOP/s"
+        src = "bf16 sustained"
+    else:
+        achieved, peak, unit = dk["gbs"], hbm, "GB/s"
+        src = "hbm copy"
+    return {"bound": dk["bound"], "kernel": dom, "achieved": achieved, "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 3), "traffic": traffic_b,
+            "traffic_note": "ncu DRAM bytes per token (profiles/ncu_traffic.json) x tokens of one launch",
+            "peak_source": f"{res['peaks']['source']} ({src})"}
 
 
 def main():
@@ -214,6 +544,8 @@ def main():
     ap.add_argument("--sentences", type=int, default=0, help="sentences per GPU per step (default: workload's)")
     ap.add_argument("--no-gather", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-side-runs", action="store_true", help="skip the other workloads' short runs")
+    ap.add_argument("--no-reference-cuda", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--lanes", type=int, default=2, choices=[1, 2],
                     help="compute lanes: alternate batches over this many workspaces / streams")
@@ -231,198 +563,21 @@ def main():
     import torch.distributed as dist
 
     import bbh
-    import synthetic as sy
 
     rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
-
+    bbh.set_gemm_pairs(args.gemm_pairs)
+    ctx = Ctx(rank, world, local, dev, args)
     desc, layers, packed, spec, per_gpu, batch = WORKLOADS[args.workload]
     n = args.sentences or per_gpu
-    weights = sy.random_weights(0, layers)
-    bbh.set_gemm_pairs(args.gemm_pairs)
-    gw = bbh.ModelWeights.from_numpy(weights, layers, local)
-
-    lengths = make_lengths(spec, n, seed=3 + 7919 * rank)
-    corpus = sy.bucketed_corpus(lengths, batch, seed=3 + 104729 * rank)
-    max_tokens = max(b.tokens for b in corpus.batches)
-    max_len = int(lengths.max())
-    if not packed:
-        S = spec[2]
-        max_tokens = batch * S
-        max_len = S
-    ws = bbh.Workspace(gw, max_tokens, batch, max_len)
-    lanes = [ws] + [bbh.Workspace(gw, max_tokens, batch, max_len) for _ in range(args.lanes - 1)]
-    ws.set_corpus_lanes(args.lanes)
-
-    i32 = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.int32, device=dev)
-    emb = torch.empty((n, 384), dtype=torch.float16, device=dev)
-    if packed:
-        d_ids, d_types = i32(corpus.ids), i32(corpus.types)
-        d_cu = [i32(b.cu) for b in corpus.batches]
-    else:
-        S = spec[2]
-        L = spec[1]
-        pid = np.zeros((n, S), np.int32)
-        pid[:, :L] = sy.sentence_tokens(np.full(n, L, np.int32), 3 + rank).reshape(n, L)
-        pmask = np.zeros((n, S), np.int32)
-        pmask[:, :L] = 1
-        d_ids, d_types, d_mask = i32(pid), i32(np.zeros_like(pid)), i32(pmask)
-    stream = torch.cuda.current_stream(dev)
-    lane_streams = [stream] + [torch.cuda.Stream(dev) for _ in range(args.lanes - 1)]
-
-    def forward_all(nlanes=None):
-        # batch bi runs on lane bi % nlanes (its own workspace and stream); the current
-        # stream orders the lanes' work before and after
-        nl = nlanes or len(lanes)
-        for ls in lane_streams[1:nl]:
-            ls.wait_stream(stream)
-        for bi, b in enumerate(corpus.batches):
-            out = emb[b.first:b.first + b.count]
-            lw, lst = lanes[bi % nl], lane_streams[bi % nl]
-            if packed:
-                lw.embed_varlen(d_ids[b.tok_start:b.tok_start + b.tokens], d_types[b.tok_start:b.tok_start + b.tokens],
-                                d_cu[bi], b.max_len, out=out, stream=lst)
-            else:
-                lw.embed(d_ids[b.first:b.first + b.count], d_types[b.first:b.first + b.count],
-                         d_mask[b.first:b.first + b.count], out=out, stream=lst)
-        for ls in lane_streams[1:nl]:
-            stream.wait_stream(ls)
-
-    gather = world > 1 and not args.no_gather
-    gathered = torch.empty((world * n, 384), dtype=torch.float16, device=dev) if gather else None
-
-    def step():
-        forward_all()
-        if gather:
-            dist.all_gather_into_tensor(gathered, emb)
-
-    def sync_all():
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    # ---------------- device-resident timed region ----------------
-    for _ in range(args.warmup):
-        step()
-    if ws.device_error() != 0:
-        raise RuntimeError("device flagged an input error")
-    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
-                          if os.environ.get("CUDA_VISIBLE_DEVICES") else local)
-    sync_all()
-    clocks.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    sync_all()
-    clock_info = clocks.stop()
-    ms = max_over_ranks(e0.elapsed_time(e1))
-    total_sentences = n * world * args.steps
-    value = total_sentences / (ms / 1000.0)
-    launches = args.steps * len(corpus.batches) * ws.launches_per_forward
-
-    # ---------------- end to end through the public API, host buffers ----------------
-    # Packed workloads: bbh_embed_corpus over the host corpus (pinned double-buffered
-    # staging, H2D of ids/types/cu_seqlens, one graph replay per batch, D2H of the
-    # embeddings to corpus order), timed on the host around the call, which returns when
-    # every embedding is in host memory. Padded workloads: bbh_embed_padded (the same
-    # staging around one bert_embed per batch of consecutive sentences).
-    h2d = d2h = 0
-    if packed:
-        # the synthetic corpus stores its sentences length-sorted: sentence i has length
-        # lengths[corpus.order[i]]
-        offsets = np.zeros(n + 1, np.int64)
-        offsets[1:] = np.cumsum(lengths[corpus.order])
-        plan = bbh.plan_batches(np.diff(offsets).astype(np.int32), batch, max_tokens, 1)
-        h_emb_np = np.zeros((n, 384), np.float16)
-        host_ids, host_types = np.ascontiguousarray(corpus.ids), np.ascontiguousarray(corpus.types)
-
-        def e2e_step():
-            ws.embed_corpus(host_ids, host_types, offsets, plan, out=h_emb_np)
-
-        sent_len = np.diff(offsets)
-        for _, idx in plan.batches():
-            h2d += 8 * int(sent_len[idx].sum()) + 4 * (len(idx) + 1)
-        d2h = 768 * n
-    else:
-        host_ids = np.ascontiguousarray(pid, dtype=np.int32)
-        host_types = np.zeros_like(host_ids)
-        host_mask = np.ascontiguousarray(pmask, dtype=np.int32)
-        h_emb_np = np.zeros((n, 384), np.float16)
-
-        def e2e_step():
-            # bert_embed per batch of the padded host corpus as one library call: pinned staging, copy
-            # streams and compute lanes inside bbh_embed_padded
-            ws.embed_padded(host_ids, host_types, host_mask, batch, out=h_emb_np)
-
-        h2d = 12 * n * spec[2]
-        d2h = 768 * n
-
-    e2e_step()
-    sync_all()
-    e2e_steps = max(1, min(args.steps, 5))
-    t0 = time.perf_counter()
-    for i in range(e2e_steps):
-        e2e_step()
-    sync_all()
-    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0) / e2e_steps
-    e2e_value = n * world / (e2e_ms / 1000.0)
-
-    # ---------------- per-kernel timing pass (same workload, eager, CUDA events) ----------------
-    ws.set_kernel_timing(True)
-    tok_per_step = int(sum(b.tokens for b in corpus.batches)) if packed else n * spec[2]
-    kt_steps = 1
-    for _ in range(kt_steps):
-        forward_all(nlanes=1)
-    kt = ws.kernel_times()
-    ws.set_kernel_timing(False)
-    hbm, tf_burst, tf_sust, peak_src = measured_peaks()
-    per_kernel = {}
-    for k, (kms, cnt) in kt.items():
-        if cnt == 0:
-            continue
-        entry = {"ms_total": round(kms, 3), "launches": int(cnt), "us_per_launch": round(1000 * kms / cnt, 2)}
-        toks = tok_per_step * kt_steps
-        if k in GEMM_NK:
-            N, K = GEMM_NK[k]
-            entry["tflops"] = round(2.0 * toks * layers * N * K / (kms / 1000.0) / 1e12, 1)
-        elif k in MEM_BYTES:
-            entry["gbs"] = round(MEM_BYTES[k] * toks * (layers if k == "attention" else 1) / (kms / 1000.0) / 1e9, 1)
-        per_kernel[k] = entry
-    total_k = sum(v["ms_total"] for v in per_kernel.values())
-    for v in per_kernel.values():
-        v["share"] = round(v["ms_total"] / total_k, 3)
-    dom = max(per_kernel, key=lambda k: per_kernel[k]["ms_total"])
-    dk = per_kernel[dom]
-    traffic = profiled_traffic()
-    if dom in GEMM_NK:
-        N, K = GEMM_NK[dom]
-        achieved = dk["tflops"]
-        peak = tf_sust
-        unit, bound = "TFLOP/s", "tensor"
-        tr = traffic.get(dom)
-        traffic_b = round(tr["bytes_per_token"] * tok_per_step * kt_steps / dk["launches"]) if tr else None
-    else:
-        achieved = dk["gbs"]
-        peak = hbm
-        unit, bound = "GB/s", "hbm"
-        tr = traffic.get(dom)
-        traffic_b = round(tr["bytes_per_token"] * tok_per_step * kt_steps / dk["launches"]) if tr else None
-    roofline = {"bound": bound, "kernel": dom, "achieved": achieved, "peak": peak, "unit": unit,
-                "frac": round(achieved / peak, 3), "traffic": traffic_b,
-                "peak_source": f"{peak_src} ({'bf16 sustained' if bound == 'tensor' else 'hbm copy'})"}
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(int(vis.split(",")[local]) if vis else local)
+    gather = not args.no_gather
+    res = measure(ctx, args.workload, n, args.steps, args.warmup, max(1, min(args.steps, 5)), gather=gather,
+                  clocks=clocks)
 
     # ---------------- CPU baseline (rank 0, N = 1) ----------------
     cpu = None
@@ -430,34 +585,48 @@ def main():
         r, cores, sample = cpu_forward_rate(args.workload, args.cpu_seconds)
         cpu = {"value": round(r, 2), "unit": "sentences/s", "cores": cores, "kind": "port", "sample": sample}
 
+    # ---------------- the other workloads, short runs (N = 1) ----------------
+    side = {}
+    if world == 1 and not args.no_side_runs:
+        for wl, ns in SIDE_RUNS.items():
+            if wl == args.workload:
+                continue
+            r2 = measure(ctx, wl, ns, 5, 3, 2, gather=gather)
+            gemm_frac = {k: r2["kernels"][k]["tensor_frac"] for k in GEMM_NK if k in r2["kernels"]}
+            side[wl] = {"workload": WORKLOADS[wl][0], "value": round(r2["value"], 1), "unit": "sentences/s",
+                        "ms_per_step": round(r2["ms"] / r2["steps"], 3), "sentences_per_step": r2["n_global"],
+                        "e2e": r2["e2e"], "gemm_frac": gemm_frac,
+                        "gemm_frac_note": "achieved FLOP/s / measured sustained bf16 peak, per GEMM kind",
+                        "kernels": r2["kernels"]}
+
     if rank == 0:
-        mean_len = float(lengths.mean()) if packed else float(spec[1])
         line = {
-            "metric": "sentences/s", "value": round(value, 1), "unit": "sentences/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+            "metric": "sentences/s", "value": round(res["value"], 1), "unit": "sentences/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(res["ms"] / args.steps, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded random-init MiniLM weights; token ids U[1000,30521] with [CLS]/[SEP])",
             "config": {
                 "workload": f"{args.workload}: {desc}", "layers": layers, "sentences_per_gpu": n,
-                "global_sentences_per_step": n * world, "batch": batch, "mean_len": round(mean_len, 2),
-                "tokens_per_gpu_step": tok_per_step, "packed": packed, "parallelism": f"dp{world} (batch-sharded replicas)",
-                "gather": "NCCL all_gather of fp16 embeddings each step" if gather else "none",
+                "global_sentences_per_step": res["n_global"], "batch": batch, "mean_len": round(res["mean_len"], 2),
+                "tokens_per_gpu_step": res["tok_per_pass"], "packed": packed,
+                "parallelism": f"dp{world} (one corpus planned over {world} ranks, LPT on FLOPs)" if packed else
+                               f"dp{world} (batch-sharded replicas)",
+                "gather": ("NCCL gather of the fp16 embeddings to rank 0 + index copy to corpus order, every step"
+                           if gather else "none"),
                 "l2": "inputs larger than L2 (each step streams ~1 GB of activations per GPU)",
                 "graph": "one CUDA graph per workspace, re-pointed per batch",
                 "lanes": f"{args.lanes} (batches alternate over {args.lanes} workspaces / streams)",
                 "gemm_tiles": ["one SM per 128-row tile", "SM pairs, 256x192", "SM pairs, 256x256 where N allows"][args.gemm_pairs],
             },
-            "roofline": roofline,
-            "kernels": per_kernel,
+            "roofline": roofline_of(res, layers),
+            "kernels": res["kernels"],
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 1), "unit": "sentences/s", "h2d_bytes_per_step": int(h2d),
-                    "d2h_bytes_per_step": int(d2h), "steps": e2e_steps,
-                    "note": ("bbh_embed_corpus: host corpus -> pinned double-buffered staging -> H2D -> forward -> "
-                             "D2H to corpus order, host-timed around the call" if packed else
-                             "bbh_embed_padded: host ids/types/mask -> pinned double-buffered staging -> H2D -> bert_embed per batch -> D2H, host-timed around the call")},
-            "gpu_launches": int(launches),
-            "clocks": clock_info,
+            "e2e": res["e2e"],
+            "gpu_launches": int(res["launches"]),
+            "clocks": res["clocks"],
         }
+        if side:
+            line["workloads"] = side
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -45,7 +45,7 @@ _SIGS = {
     "bbh_ws_create": (_I, [_P, _I, _I, _I, ctypes.POINTER(_P)]),
     "bbh_ws_free": (None, [_P]),
     "bbh_ws_set_graph": (_I, [_P, _I]),
-    "bbh_ws_set_ffn_fusion": (_I, [_P, _I]),
+    "bbh_ws_set_gemm_pairs": (_I, [_P, _I]),
     "bbh_ws_set_pdl": (_I, [_P, _I]),
     "bbh_set_gemm_pairs": (_I, [_I]),
     "bbh_device_error": (_I, [_P, _I]),
@@ -59,11 +59,12 @@ _SIGS = {
     "bbh_linear": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "bbh_linear_residual_layernorm": (_I, [_P, _P, _P, _P, _P, _P, ctypes.c_float, _P, _I, _I, _P]),
     "bbh_layernorm": (_I, [_P, _P, _P, _P, _I, _I, ctypes.c_float, _P, _P]),
-    "bbh_ffn_block": (_I, [_P, _P, _P, _P, _P, _P, _P, ctypes.c_float, _P, _I, _P]),
     "bbh_attention_varlen": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bbh_mean_pool_l2": (_I, [_P, _P, _P, _I, _P, _P]),
     "bbh_plan_batches": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, ctypes.POINTER(_I)]),
+    "bbh_embed_gather_indices": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "bbh_embed_corpus": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _P, _P]),
+    "bbh_embed_corpus_device": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _P, _P]),
     "bbh_embed_padded": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
     "bbh_ws_set_corpus_lanes": (_I, [_P, _I]),
     "bbh_vocab_load": (_I, [ctypes.c_char_p, _I, ctypes.POINTER(_P)]),
@@ -208,11 +209,12 @@ class Workspace:
     def set_pdl(self, enable: bool):
         _check(lib().bbh_ws_set_pdl(self.handle, 1 if enable else 0))
 
-    def set_ffn_fusion(self, enable: bool):
-        _check(lib().bbh_ws_set_ffn_fusion(self.handle, 1 if enable else 0))
+    KERNEL_KINDS = ("embed_ln", "qkv_gemm", "attention", "o_gemm_ln", "ffn1_gemm_gelu", "ffn2_gemm_ln", "pool_l2")
 
-    KERNEL_KINDS = ("embed_ln", "qkv_gemm", "attention", "o_gemm_ln", "ffn1_gemm_gelu", "ffn2_gemm_ln", "pool_l2",
-                    "ffn_fused")
+    def set_gemm_pairs(self, mode: int):
+        """GEMM tiles of this workspace's forwards: 0 = one SM per 128-row tile, 1 = SM pairs
+        (256 x 192 where N allows, else 256 x 256), 2 = SM pairs, 256 x 256 first."""
+        _check(lib().bbh_ws_set_gemm_pairs(self.handle, int(mode)))
 
     def set_kernel_timing(self, enable: bool):
         _check(lib().bbh_ws_set_kernel_timing(self.handle, 1 if enable else 0))
@@ -269,6 +271,21 @@ class Workspace:
                                        B, T, max_len, _f16(out), _f16(dump), _stream(stream)))
         return (out, dump) if dump_layers else out
 
+    def gather_indices(self, ids, types=None, mask=None, cu_seqlens=None, max_len: int = 0, stream=None):
+        """(word id, position, type id, mask) per token, as the embedding kernel resolves them:
+        int32 CUDA tensor [T, 4]. Packed when cu_seqlens is given (ids [T]), else padded
+        (ids [B, S])."""
+        if cu_seqlens is not None:
+            T, B, S = ids.shape[0], cu_seqlens.shape[0] - 1, 0
+        else:
+            B, S = ids.shape
+            T = B * S
+        out = torch.empty((max(T, 1), 4), dtype=torch.int32, device=ids.device)
+        _check(lib().bbh_embed_gather_indices(self.handle, self.weights.handle, _i32(ids), _i32(types), _i32(mask),
+                                              _i32(cu_seqlens), B, S, T, max_len, ctypes.c_void_p(out.data_ptr()),
+                                              _stream(stream)))
+        return out[:T]
+
     # ---- host corpus -------------------------------------------------------------------
     def embed_corpus(self, ids, types, offsets, plan: "CorpusPlan", rank: int = 0, out=None, stream=None):
         """Runs the plan's batches of `rank` from HOST numpy arrays (ids/types int32 of all
@@ -286,6 +303,25 @@ class Workspace:
         _check(lib().bbh_embed_corpus(self.handle, self.weights.handle, p(ids), p(types), p(offsets), n,
                                       p(plan.order), p(plan.batch_first), p(plan.batch_rank), plan.n_batches,
                                       rank, p(out), _stream(stream)))
+        return out
+
+    def embed_corpus_device(self, ids, types, offsets, plan: "CorpusPlan", rank: int = 0, out=None, stream=None):
+        """The same loop with the embeddings left on the device: returns a CUDA fp16 [m, 384]
+        tensor holding the m sentences of `rank`'s batches in plan order (corpus indices:
+        plan.rank_order(rank)), ready for a collective."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        types = None if types is None else np.ascontiguousarray(types, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.int64)
+        n = offsets.size - 1
+        m = int(plan.rank_order(rank).size)
+        if out is None:
+            out = torch.empty((max(m, 1), HIDDEN), dtype=torch.float16, device=f"cuda:{self.weights.device}")
+        if out.dtype != torch.float16 or out.shape[0] < m or out.shape[1] != HIDDEN or not out.is_contiguous():
+            raise ValueError("out must be a contiguous CUDA float16 [>= m, 384] tensor")
+        p = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+        _check(lib().bbh_embed_corpus_device(self.handle, self.weights.handle, p(ids), p(types), p(offsets), n,
+                                             p(plan.order), p(plan.batch_first), p(plan.batch_rank), plan.n_batches,
+                                             rank, ctypes.c_void_p(out.data_ptr()), _stream(stream)))
         return out
 
     def embed_padded(self, ids, types, mask, batch: int, out=None, stream=None):
@@ -380,6 +416,11 @@ class CorpusPlan:
     def __init__(self, order, batch_first, batch_rank, n_batches):
         self.order, self.batch_first, self.batch_rank, self.n_batches = order, batch_first, batch_rank, n_batches
 
+    def rank_order(self, rank: int) -> np.ndarray:
+        """Corpus indices of `rank`'s sentences in plan order (its batches back to back)."""
+        parts = [idx for _, idx in self.batches(rank)]
+        return np.concatenate(parts) if parts else np.zeros(0, np.int32)
+
     def batches(self, rank=None):
         for b in range(self.n_batches):
             if rank is None or self.batch_rank[b] == rank:
@@ -427,9 +468,9 @@ def spearman(x, y) -> float:
 
 # ---- unit operators ---------------------------------------------------------------------
 def set_gemm_pairs(mode: int) -> None:
-    """Tile shape of the bias / GELU projections in plans built from now on (process-wide):
-    0 = one SM per 128-row tile, 1 = SM pairs (256 x 192 where N allows, else 256 x 256),
-    2 = SM pairs, 256 x 256 first."""
+    """Process-wide default GEMM tile mode for the unit operators and for workspaces created
+    afterwards (Workspace.set_gemm_pairs sets one workspace's): 0 = one SM per 128-row tile,
+    1 = SM pairs (256 x 192 where N allows, else 256 x 256), 2 = SM pairs, 256 x 256 first."""
     _check(lib().bbh_set_gemm_pairs(int(mode)))
 
 
@@ -448,14 +489,6 @@ def linear_residual_layernorm(A, W, bias, residual, gamma, beta, eps=1e-12, stre
     _check(lib().bbh_linear_residual_layernorm(_f16(A), _f16(W), _f16(bias), _f16(residual), _f16(gamma),
                                                _f16(beta), eps, _f16(C), M, K, _stream(stream)))
     return C
-
-
-def ffn_block(Y, W1, b1, W2, b2, gamma, beta, eps=1e-12, stream=None):
-    """ffn_block: LN(GELU(Y W1^T + b1) W2^T + b2 + Y) * gamma + beta in one fused kernel."""
-    out = torch.empty_like(Y)
-    _check(lib().bbh_ffn_block(_f16(Y), _f16(W1), _f16(b1), _f16(W2), _f16(b2), _f16(gamma), _f16(beta), eps,
-                               _f16(out), Y.shape[0], _stream(stream)))
-    return out
 
 
 def layernorm(x, gamma, beta, eps=1e-12, residual=None, stream=None):

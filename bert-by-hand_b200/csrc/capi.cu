@@ -289,8 +289,7 @@ struct bbh_ws {
   int32_t* meta = nullptr;
   int* err = nullptr;
   std::vector<GemmPlan> plans;  // 4 per layer: QKV, O+LN, FFN1+GELU, FFN2+LN
-  std::vector<bbh::MlpPlan> mlp_plans;  // per layer: the fused FFN block
-  bool fused_ffn = false;               // measured slower than the two GEMMs (see mlp_fused.cu)
+  int gemm_pairs = 1;           // make_gemm_plan's pair_mode for this workspace's plans
   bool pdl = true;                      // programmatic dependent launch between the forward's kernels
   bool use_graph = true;
   cudaStream_t cap_stream = nullptr;
@@ -331,15 +330,21 @@ namespace {
 int build_plans(bbh_ws* ws, const bbh_weights* w) {
   using namespace bbh;
   ws->plans.assign(size_t(w->layers) * 4, GemmPlan{});
-  ws->mlp_plans.assign(size_t(w->layers), MlpPlan{});
+  const int pm = ws->gemm_pairs;
   for (int l = 0; l < w->layers; ++l) {
     const LayerPtrs& L = w->L[l];
     GemmPlan* P = &ws->plans[size_t(l) * 4];
     const int T = ws->max_tokens;
-    int rc = make_gemm_plan(&P[0], ws->X, kHidden, T, L.qkv_w, kQkvLd, kHidden, ws->qkv, kQkvLd, kEpiBias, ws->num_sms);
-    if (!rc) rc = make_gemm_plan(&P[1], ws->ctx, kHidden, T, L.o_w, kHidden, kHidden, ws->Y, kHidden, kEpiResLN, ws->num_sms);
-    if (!rc) rc = make_gemm_plan(&P[2], ws->Y, kHidden, T, L.i_w, kFfn, kHidden, ws->inter, kFfn, kEpiGelu, ws->num_sms);
-    if (!rc) rc = make_gemm_plan(&P[3], ws->inter, kFfn, T, L.o2_w, kHidden, kFfn, ws->X, kHidden, kEpiResLN, ws->num_sms);
+    int rc = make_gemm_plan(&P[0], ws->X, kHidden, T, L.qkv_w, kQkvLd, kHidden, ws->qkv, kQkvLd, kEpiBias,
+                            ws->num_sms, pm);
+    if (!rc)
+      rc = make_gemm_plan(&P[1], ws->ctx, kHidden, T, L.o_w, kHidden, kHidden, ws->Y, kHidden, kEpiResLN, ws->num_sms,
+                          pm);
+    if (!rc)
+      rc = make_gemm_plan(&P[2], ws->Y, kHidden, T, L.i_w, kFfn, kHidden, ws->inter, kFfn, kEpiGelu, ws->num_sms, pm);
+    if (!rc)
+      rc = make_gemm_plan(&P[3], ws->inter, kFfn, T, L.o2_w, kHidden, kFfn, ws->X, kHidden, kEpiResLN, ws->num_sms,
+                          pm);
     if (!rc) rc = set_gemm_residual(&P[1], ws->X, kHidden);
     if (!rc) rc = set_gemm_residual(&P[3], ws->Y, kHidden);
     if (rc) return fail(rc, "tensor map encoding failed");
@@ -349,15 +354,6 @@ int build_plans(bbh_ws* ws, const bbh_weights* w) {
     P[2].p.C = ws->inter; P[2].p.ldc = kFfn; P[2].p.bias = L.i_b;
     P[3].p.C = ws->X;    P[3].p.ldc = kHidden; P[3].p.bias = L.o2_b;
     P[3].p.gamma = L.ln2_g; P[3].p.beta = L.ln2_b;
-    MlpPlan& M = ws->mlp_plans[size_t(l)];
-    rc = make_mlp_plan(&M, ws->Y, T, L.i_w, L.o2_w, ws->X, ws->num_sms);
-    if (rc) return fail(rc, "tensor map encoding failed (FFN block)");
-    M.p.b1 = L.i_b;
-    M.p.b2 = L.o2_b;
-    M.p.gamma = L.ln2_g;
-    M.p.beta = L.ln2_b;
-    M.p.rows_dev = ws->meta + 1;
-    M.p.err = ws->err;
     for (int j = 0; j < 4; ++j) {
       P[j].p.rows_dev = ws->meta + 1;
       P[j].p.err = ws->err;
@@ -440,14 +436,9 @@ int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh
       KernelMark km(ws, s, 3);
       BBH_CUDA(launch_gemm(P[1], s, ws->pdl));
     }
-    if (ws->fused_ffn) {
-      KernelMark km(ws, s, 7);
-      BBH_CUDA(launch_mlp(ws->mlp_plans[size_t(l)], s, ws->pdl));
-    } else {
-      for (int j = 2; j < 4; ++j) {
-        KernelMark km(ws, s, 2 + j);
-        BBH_CUDA(launch_gemm(P[j], s, ws->pdl));
-      }
+    for (int j = 2; j < 4; ++j) {
+      KernelMark km(ws, s, 2 + j);
+      BBH_CUDA(launch_gemm(P[j], s, ws->pdl));
     }
     if (dump) BBH_CUDA(cudaMemcpyAsync(dump + plane * (l + 1), ws->X, plane * 2, cudaMemcpyDeviceToDevice, s));
   }
@@ -593,6 +584,7 @@ int bbh_ws_create(const bbh_weights* w, int max_tokens, int max_batch, int max_l
   ws->max_tokens = max_tokens;
   ws->max_batch = max_batch;
   ws->max_len = max_len;
+  ws->gemm_pairs = bbh::default_gemm_pair_mode();
   const size_t T = size_t(max_tokens);
   size_t sizes[9] = {T * kHidden * 2, T * kHidden * 2, T * kQkvLd * 2, T * kHidden * 2, T * kFfn * 2,
                      T, size_t(max_batch + 1) * 4, 16, 16};
@@ -655,18 +647,20 @@ int bbh_ws_set_corpus_lanes(bbh_ws* ws, int lanes) {
   return BBH_OK;
 }
 
-int bbh_ws_set_ffn_fusion(bbh_ws* ws, int enable) {
-  if (!ws) return fail(BBH_ERR_ARG, "null workspace");
-  if ((enable != 0) != ws->fused_ffn) {
-    ws->fused_ffn = enable != 0;
-    drop_graph(ws);  // the captured graph holds the other launch sequence
-  }
+int bbh_set_gemm_pairs(int mode) {
+  if (mode < 0 || mode > 2) return fail(BBH_ERR_ARG, "bbh_set_gemm_pairs: mode must be 0, 1 or 2");
+  bbh::set_default_gemm_pair_mode(mode);
   return BBH_OK;
 }
 
-int bbh_set_gemm_pairs(int mode) {
-  if (mode < 0 || mode > 2) return fail(BBH_ERR_ARG, "bbh_set_gemm_pairs: mode must be 0, 1 or 2");
-  bbh::g_gemm_pair_mode = mode;
+int bbh_ws_set_gemm_pairs(bbh_ws* ws, int mode) {
+  if (!ws) return fail(BBH_ERR_ARG, "null workspace");
+  if (mode < 0 || mode > 2) return fail(BBH_ERR_ARG, "bbh_ws_set_gemm_pairs: mode must be 0, 1 or 2");
+  if (mode != ws->gemm_pairs) {
+    ws->gemm_pairs = mode;
+    drop_graph(ws);
+    ws->w = nullptr;  // the plans are rebuilt with the new tiles by the next forward
+  }
   return BBH_OK;
 }
 
@@ -710,7 +704,7 @@ int bbh_ws_kernel_times(bbh_ws* ws, double* ms, int64_t* counts) {
 
 int bbh_launches_per_forward(const bbh_ws* ws) {
   if (!ws || !ws->w) return 0;
-  const int per_layer = (ws->max_len > bbh::kAttnTcMaxLen ? 6 : 5) - (ws->fused_ffn ? 1 : 0);
+  const int per_layer = ws->max_len > bbh::kAttnTcMaxLen ? 6 : 5;
   return 2 + per_layer * ws->w->layers;
 }
 
@@ -790,6 +784,36 @@ int bbh_encode_varlen(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, cons
   return encode_common(ws, ep, out, layer_dump, static_cast<cudaStream_t>(stream));
 }
 
+int bbh_embed_gather_indices(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
+                             const int32_t* mask, const int32_t* cu_seqlens, int batch, int seq, int total_tokens,
+                             int max_len, int32_t* indices, void* stream) {
+  int rc = prepare(ws, w);
+  if (rc) return rc;
+  if (!indices || (reinterpret_cast<uintptr_t>(indices) & 15))
+    return fail(BBH_ERR_ARG, "bbh_embed_gather_indices: indices must be a 16-byte aligned [T, 4] int32 array");
+  bbh::EmbedParams ep = base_embed_params(ws, w);
+  ep.ids = ids;
+  ep.types = types;
+  ep.batch = batch;
+  if (cu_seqlens) {
+    rc = check_packed(ws, ids, cu_seqlens, indices, batch, total_tokens, max_len);
+    if (rc) return rc;
+    ep.cu_seqlens = cu_seqlens;
+    ep.total = total_tokens;
+    ep.max_len = max_len;
+  } else {
+    rc = check_padded(ws, ids, indices, batch, seq);
+    if (rc) return rc;
+    ep.mask = mask;
+    ep.seq = seq;
+    ep.total = batch * seq;
+    ep.max_len = seq;
+  }
+  ep.index_dump = indices;
+  BBH_CUDA(bbh::launch_embed_ln(ep, ws->num_sms * 8, static_cast<cudaStream_t>(stream)));
+  return BBH_OK;
+}
+
 // ---------------------------------------------------------------------- unit operators
 
 static int current_device(int* dev) {
@@ -812,7 +836,7 @@ static int unit_gemm(const uint16_t* A, const uint16_t* W, const uint16_t* bias,
   if (rc) return rc;
   GemmPlan plan;
   rc = make_gemm_plan(&plan, reinterpret_cast<const __half*>(A), K, M, reinterpret_cast<const __half*>(W), N, K,
-                      reinterpret_cast<__half*>(C), N, epi, g_num_sms(dev));
+                      reinterpret_cast<__half*>(C), N, epi, g_num_sms(dev), default_gemm_pair_mode());
   if (rc) return fail(rc, "bbh_linear: unsupported shape or alignment (N, K must be multiples of 8)");
   plan.p.C = reinterpret_cast<__half*>(C);
   plan.p.ldc = N;
@@ -841,31 +865,6 @@ int bbh_linear_residual_layernorm(const uint16_t* A, const uint16_t* W, const ui
                                   const uint16_t* residual, const uint16_t* gamma, const uint16_t* beta, float eps,
                                   uint16_t* C, int M, int K, void* stream) {
   return unit_gemm(A, W, bias, residual, gamma, beta, eps, C, M, bbh::kHidden, K, bbh::kEpiResLN, stream);
-}
-
-int bbh_ffn_block(const uint16_t* Y, const uint16_t* W1, const uint16_t* b1, const uint16_t* W2, const uint16_t* b2,
-                  const uint16_t* gamma, const uint16_t* beta, float eps, uint16_t* out, int M, void* stream) {
-  using namespace bbh;
-  if (!Y || !W1 || !b1 || !W2 || !b2 || !gamma || !beta || !out || M <= 0)
-    return fail(BBH_ERR_ARG, "bbh_ffn_block: bad arguments");
-  if ((reinterpret_cast<uintptr_t>(Y) | reinterpret_cast<uintptr_t>(out)) & 15)
-    return fail(BBH_ERR_ARG, "bbh_ffn_block: pointers must be 16-byte aligned");
-  int dev = 0;
-  int rc = current_device(&dev);
-  if (rc) return rc;
-  MlpPlan plan;
-  rc = make_mlp_plan(&plan, reinterpret_cast<const __half*>(Y), M, reinterpret_cast<const __half*>(W1),
-                     reinterpret_cast<const __half*>(W2), reinterpret_cast<__half*>(out), g_num_sms(dev));
-  if (rc) return fail(rc, "bbh_ffn_block: tensor map encoding failed (alignment)");
-  plan.p.b1 = reinterpret_cast<const __half*>(b1);
-  plan.p.b2 = reinterpret_cast<const __half*>(b2);
-  plan.p.gamma = reinterpret_cast<const __half*>(gamma);
-  plan.p.beta = reinterpret_cast<const __half*>(beta);
-  plan.p.eps = eps;
-  plan.p.rows = M;
-  plan.p.err = unit_err_word(dev);
-  BBH_CUDA(launch_mlp(plan, static_cast<cudaStream_t>(stream)));
-  return BBH_OK;
 }
 
 int bbh_layernorm(const uint16_t* x, const uint16_t* gamma, const uint16_t* beta, uint16_t* y, int M, int D,
@@ -952,12 +951,13 @@ static __device__ __align__(256) unsigned char g_bbh_static_scratch[kStBytes];
 
 namespace {
 
+std::mutex g_static_mu;
+
 // Device address of g_bbh_static_scratch on `device` (looked up with that device current).
 int static_scratch(int device, uint8_t** out) {
-  static std::mutex mu;
   static uint8_t* addr[64] = {};
   if (device < 0 || device >= 64) return fail(BBH_ERR_ARG, "bad device ordinal");
-  std::lock_guard<std::mutex> lk(mu);
+  std::lock_guard<std::mutex> lk(g_static_mu);
   if (!addr[device]) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_bbh_static_scratch);
@@ -965,6 +965,33 @@ int static_scratch(int device, uint8_t** out) {
     addr[device] = static_cast<uint8_t*>(p);
   }
   *out = addr[device];
+  return BBH_OK;
+}
+
+// GEMM plans (tensor maps over the static array and a weight arena) cached per device, so
+// a call re-encodes them only when it is given a different weight arena. The arena's
+// address and layer count determine every weight pointer, so they are the cache key.
+struct StaticPlans {
+  const __half* arena = nullptr;
+  int layers = 0;
+  std::vector<GemmPlan> plans;
+};
+
+int static_plans(bbh_ws* ws, const bbh_weights* w) {
+  static StaticPlans cache[64];
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  StaticPlans& c = cache[ws->device];
+  if (c.arena != w->arena || c.layers != w->layers) {
+    c.arena = nullptr;
+    const int rc = build_plans(ws, w);
+    if (rc) return rc;
+    c.plans = ws->plans;
+    c.arena = w->arena;
+    c.layers = w->layers;
+    return BBH_OK;
+  }
+  ws->plans = c.plans;
+  ws->w = w;
   return BBH_OK;
 }
 
@@ -994,7 +1021,7 @@ int bbh_embed_varlen_static(const bbh_weights* w, const int32_t* ids, const int3
   ws.num_sms = g_num_sms(w->device);
   ws.max_tokens = BBH_STATIC_MAX_TOKENS;
   ws.max_batch = BBH_STATIC_MAX_BATCH;
-  ws.max_len = BBH_MAX_POSITIONS;
+  ws.max_len = max_len;  // the long-sentence attention kernel runs only when a sentence can need it
   ws.X = reinterpret_cast<__half*>(base + kStOffX);
   ws.Y = reinterpret_cast<__half*>(base + kStOffY);
   ws.qkv = reinterpret_cast<__half*>(base + kStOffQkv);
@@ -1005,7 +1032,7 @@ int bbh_embed_varlen_static(const bbh_weights* w, const int32_t* ids, const int3
   ws.meta = reinterpret_cast<int32_t*>(base + kStOffMeta);
   ws.err = reinterpret_cast<int*>(base + kStOffErr);
   ws.use_graph = false;
-  rc = build_plans(&ws, w);
+  rc = static_plans(&ws, w);
   if (rc) return rc;
 
   // The error word must start at zero; everything else is written before it is read.

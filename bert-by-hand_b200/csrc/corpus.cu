@@ -207,40 +207,49 @@ int bbh_plan_batches(const int32_t* lengths, int n, int max_batch, int max_token
   return BBH_OK;
 }
 
-int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
-                     const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
-                     const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// The corpus loop of bbh_embed_corpus (emb: host rows in corpus order) and of
+// bbh_embed_corpus_device (emb_dev: device rows, this rank's sentences in plan order).
+int corpus_run(const char* who, bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
+               const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
+               const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb, uint16_t* emb_dev, void* stream) {
+  const std::string name(who);
   if (!ws || !w || !offsets || n < 0 || n_batches < 0 || !batch_first || (n_batches > 0 && (!order || !batch_rank)) ||
-      (n > 0 && (!ids || !emb)))
-    return bbh::internal_fail(BBH_ERR_ARG, "bbh_embed_corpus: bad arguments");
+      (n > 0 && (!ids || (!emb && !emb_dev))))
+    return bbh::internal_fail(BBH_ERR_ARG, name + ": bad arguments");
+  if (emb_dev && (reinterpret_cast<uintptr_t>(emb_dev) & 15))
+    return bbh::internal_fail(BBH_ERR_ARG, name + ": the device output must be 16-byte aligned");
   if (batch_first[0] != 0 || batch_first[n_batches] != n)
-    return bbh::internal_fail(BBH_ERR_ARG, "bbh_embed_corpus: batch_first must run from 0 to n");
+    return bbh::internal_fail(BBH_ERR_ARG, name + ": batch_first must run from 0 to n");
   int device = 0, max_tokens = 0, max_batch = 0, max_len = 0;
   bbh::ws_limits(ws, &device, &max_tokens, &max_batch, &max_len);
   // validate the whole plan on the host before anything is queued
   for (int b = 0; b < n_batches; ++b) {
     const int lo = batch_first[b], hi = batch_first[b + 1];
     if (hi < lo || hi - lo > max_batch)
-      return bbh::internal_fail(BBH_ERR_CAPACITY, "bbh_embed_corpus: batch " + std::to_string(b) +
+      return bbh::internal_fail(BBH_ERR_CAPACITY, name + ": batch " + std::to_string(b) +
                                                       " exceeds the workspace's sentence capacity");
     int64_t tok = 0;
     for (int i = lo; i < hi; ++i) {
       const int s = order[i];
-      if (s < 0 || s >= n) return bbh::internal_fail(BBH_ERR_ARG, "bbh_embed_corpus: order out of range");
+      if (s < 0 || s >= n) return bbh::internal_fail(BBH_ERR_ARG, name + ": order out of range");
       const int64_t L = offsets[s + 1] - offsets[s];
       if (L < 0 || L > max_len)
-        return bbh::internal_fail(BBH_ERR_CAPACITY, "bbh_embed_corpus: sentence " + std::to_string(s) +
+        return bbh::internal_fail(BBH_ERR_CAPACITY, name + ": sentence " + std::to_string(s) +
                                                         " is longer than the workspace's max_len");
       tok += L;
     }
     if (tok > max_tokens)
-      return bbh::internal_fail(BBH_ERR_CAPACITY, "bbh_embed_corpus: batch " + std::to_string(b) +
+      return bbh::internal_fail(BBH_ERR_CAPACITY, name + ": batch " + std::to_string(b) +
                                                       " exceeds the workspace's token capacity");
   }
   int prev = 0;
   Stage* stp = nullptr;
   {
-    const int rc0 = acquire_stage(ws, w, &stp, &prev, "bbh_embed_corpus");
+    const int rc0 = acquire_stage(ws, w, &stp, &prev, who);
     if (rc0) {
       cudaSetDevice(prev);
       return rc0;
@@ -250,11 +259,18 @@ int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int lanes = bbh::ws_corpus_lanes(ws);
 
-  // Copies a finished slot's embeddings to their corpus rows.
+  // Copies a finished slot's embeddings to their corpus rows (host output), or waits until
+  // the slot's forward has read its inputs (device output).
   auto drain = [&](Slot& sl) -> int {
     if (sl.batch < 0) return BBH_OK;
+    if (emb_dev) {
+      sl.batch = -1;
+      if (cudaEventSynchronize(sl.fwd) != cudaSuccess)
+        return bbh::internal_fail(BBH_ERR_CUDA, name + ": forward failed");
+      return BBH_OK;
+    }
     if (cudaEventSynchronize(sl.d2h) != cudaSuccess)
-      return bbh::internal_fail(BBH_ERR_CUDA, "bbh_embed_corpus: device->host copy failed");
+      return bbh::internal_fail(BBH_ERR_CUDA, name + ": device->host copy failed");
     const int lo = batch_first[sl.batch], hi = batch_first[sl.batch + 1];
     for (int i = lo; i < hi; ++i)
       std::memcpy(emb + size_t(order[i]) * BBH_HIDDEN, sl.h_emb + size_t(i - lo) * BBH_HIDDEN,
@@ -265,6 +281,7 @@ int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const
 
   int rc = BBH_OK;
   int k = 0;
+  size_t dev_row = 0;  // device output: next row of this rank's plan-order embeddings
   for (int b = 0; b < n_batches && rc == BBH_OK; ++b) {
     if (batch_rank[b] != rank) continue;
     Slot& sl = st.slot[k & 1];
@@ -295,18 +312,28 @@ int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const
                   cudaSuccess &&
               cudaEventRecord(sl.h2d, st.up) == cudaSuccess && cudaStreamWaitEvent(ls, sl.h2d, 0) == cudaSuccess;
     if (!ok) {
-      rc = bbh::internal_fail(BBH_ERR_CUDA, "bbh_embed_corpus: host->device copy failed");
+      rc = bbh::internal_fail(BBH_ERR_CUDA, name + ": host->device copy failed");
       break;
     }
+    uint16_t* out = emb_dev ? emb_dev + dev_row * BBH_HIDDEN : sl.d_emb;
+    dev_row += size_t(count);
     rc = bbh_embed_varlen(lws, w, sl.d_ids, types ? sl.d_types : nullptr, sl.d_cu, count, tok, std::max(blen, 1),
-                          sl.d_emb, ls);
+                          out, ls);
     if (rc) break;
+    if (emb_dev) {
+      if (cudaEventRecord(sl.fwd, ls) != cudaSuccess) {
+        rc = bbh::internal_fail(BBH_ERR_CUDA, name + ": event record failed");
+        break;
+      }
+      sl.batch = b;
+      continue;
+    }
     ok = cudaEventRecord(sl.fwd, ls) == cudaSuccess && cudaStreamWaitEvent(st.down, sl.fwd, 0) == cudaSuccess &&
          cudaMemcpyAsync(sl.h_emb, sl.d_emb, size_t(count) * BBH_HIDDEN * sizeof(uint16_t), cudaMemcpyDeviceToHost,
                          st.down) == cudaSuccess &&
          cudaEventRecord(sl.d2h, st.down) == cudaSuccess;
     if (!ok) {
-      rc = bbh::internal_fail(BBH_ERR_CUDA, "bbh_embed_corpus: device->host copy failed");
+      rc = bbh::internal_fail(BBH_ERR_CUDA, name + ": device->host copy failed");
       break;
     }
     sl.batch = b;
@@ -316,9 +343,29 @@ int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const
     if (!rc) rc = r2;
     sl.batch = -1;
   }
-  if (!rc) rc = device_status(ws, st, "bbh_embed_corpus");
+  if (!rc) rc = device_status(ws, st, who);
   cudaSetDevice(prev);
   return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
+                     const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
+                     const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb, void* stream) {
+  if (n > 0 && !emb) return bbh::internal_fail(BBH_ERR_ARG, "bbh_embed_corpus: bad arguments");
+  return corpus_run("bbh_embed_corpus", ws, w, ids, types, offsets, n, order, batch_first, batch_rank, n_batches,
+                    rank, emb, nullptr, stream);
+}
+
+int bbh_embed_corpus_device(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
+                            const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
+                            const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb_dev, void* stream) {
+  if (n > 0 && !emb_dev) return bbh::internal_fail(BBH_ERR_ARG, "bbh_embed_corpus_device: bad arguments");
+  return corpus_run("bbh_embed_corpus_device", ws, w, ids, types, offsets, n, order, batch_first, batch_rank,
+                    n_batches, rank, nullptr, emb_dev, stream);
 }
 
 int bbh_embed_padded(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types, const int32_t* mask,

@@ -15,6 +15,8 @@
 //    tcgen05.ld 64 columns at a time, bias / GELU / residual + two-pass LayerNorm in
 //    fp32 (row statistics combined through shared memory), fp16 stores. Two TMEM accumulators (when 2*BN <= 512)
 //    let the MMA of tile i+1 overlap the epilogue of tile i.
+#include <atomic>
+
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "internal.h"
@@ -403,7 +405,7 @@ static cudaError_t launch_inst(const GemmPlan& plan, cudaStream_t stream, bool p
 }
 
 int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const __half* W, int N, int K,
-                   __half* C, int ldc, int epi, int num_sms) {
+                   __half* C, int ldc, int epi, int num_sms, int pair_mode) {
   if (!plan || !A || !W || !C || rows_cap <= 0 || N <= 0 || K <= 0 || N % 8 || K % 8 || lda < K || ldc < N)
     return BBH_ERR_ARG;
   int bn;
@@ -428,8 +430,8 @@ int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const
   plan->bn = bn;
   plan->bn2 = 0;
   memset(&plan->tmB2, 0, sizeof(plan->tmB2));
-  if (g_gemm_pair_mode) {
-    const int order[2] = {g_gemm_pair_mode == 2 ? 256 : 192, g_gemm_pair_mode == 2 ? 192 : 256};
+  if (pair_mode) {
+    const int order[2] = {pair_mode == 2 ? 256 : 192, pair_mode == 2 ? 192 : 256};
     for (int b2 : order)
       if (gemm_pair_supported(N, epi, b2)) {
         rc = encode_2d(&plan->tmB2, W, N, K, K, 64, b2 / 2, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -460,7 +462,9 @@ int set_gemm_residual(GemmPlan* plan, const __half* R, int ldr) {
   return encode_2d(&plan->tmR, R, plan->rows_cap, plan->p.N, ldr, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-int g_gemm_pair_mode = 1;
+static std::atomic<int> g_default_pair_mode{1};
+int default_gemm_pair_mode() { return g_default_pair_mode.load(std::memory_order_relaxed); }
+void set_default_gemm_pair_mode(int mode) { g_default_pair_mode.store(mode, std::memory_order_relaxed); }
 
 cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream, bool pdl) {
   if (plan.epi == kEpiResLN && !plan.p.residual) return cudaErrorInvalidValue;

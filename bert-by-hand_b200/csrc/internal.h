@@ -90,8 +90,10 @@ struct GemmPlan {
 // Builds the tensor maps and picks the tile shape. A: [rows_cap, K] row-major with row
 // stride lda elements; W: [N, K] row-major (nn.Linear layout); C: [rows_cap, N] with row
 // stride ldc (written by TMA stores, clipped at rows_cap and N). Returns 0 or a BBH_ERR_*.
+// pair_mode: 0 = one SM per 128-row tile; 1 = CTA pairs of 256 x 192 tiles where N allows
+// it, else 256 x 256; 2 = 256 x 256 first.
 int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const __half* W, int N, int K,
-                   __half* C, int ldc, int epi, int num_sms);
+                   __half* C, int ldc, int epi, int num_sms, int pair_mode);
 // Tensor map of a row-major [rows, cols] fp16 matrix (row stride ld elements), box
 // box_cols x box_rows with the given swizzle. Returns 0 or a BBH_ERR_*.
 int encode_2d(CUtensorMap* map, const __half* base, int rows, int cols, int ld, int box_cols, int box_rows,
@@ -102,37 +104,10 @@ cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream, bool pdl = fa
 // CTA-pair kernel (gemm_pair.cu): bias / GELU epilogues, N a multiple of the pair width.
 bool gemm_pair_supported(int N, int epi, int bn);
 cudaError_t launch_gemm_pair(const GemmPlan& plan, cudaStream_t stream, bool pdl);
-// Which kernel plans built from now on use for the bias / GELU GEMMs: 0 = one-SM tiles,
-// 1 = CTA pairs of 256 x 192 tiles where N allows it, else 256 x 256, 2 = 256 x 256 first.
-extern int g_gemm_pair_mode;
-
-// ------------------------------------------------------------------ fused FFN block
-// out = LayerNorm(GELU(Y W1^T + b1) W2^T + b2 + residual) * gamma + beta (mlp_fused.cu)
-struct MlpParams {
-  __half* C;               // [rows, ldc] output
-  int ldc;
-  const __half* residual;  // [rows, ldr]
-  int ldr;
-  const __half* b1;        // [1536]
-  const __half* b2;        // [384]
-  const __half* gamma;     // [384]
-  const __half* beta;      // [384]
-  float eps;
-  const int* rows_dev;     // when non-null the row count is read from device memory
-  int rows;
-  int* err;
-};
-struct MlpPlan {
-  CUtensorMap tmX;   // Y [rows_cap, 384]
-  CUtensorMap tmW1;  // [1536, 384]
-  CUtensorMap tmW2;  // [384, 1536]
-  MlpParams p;
-  int grid;
-};
-// Y: [rows_cap, 384] input (also the default residual); W1/W2 nn.Linear layouts; C output.
-int make_mlp_plan(MlpPlan* plan, const __half* Y, int rows_cap, const __half* W1, const __half* W2, __half* C,
-                  int num_sms);
-cudaError_t launch_mlp(const MlpPlan& plan, cudaStream_t stream, bool pdl = false);
+// Process-wide default tile mode (make_gemm_plan's pair_mode) for the unit operators and
+// for workspaces created afterwards; a workspace keeps its own copy.
+int default_gemm_pair_mode();
+void set_default_gemm_pair_mode(int mode);
 
 // ------------------------------------------------------------------ other kernels
 // Forward-call description consumed by the first kernel of a forward. It is passed by
@@ -159,6 +134,7 @@ struct EmbedParams {
   uint8_t* ws_tokmask;        // [T] 1 = real token (attends and is pooled)
   int32_t* ws_meta;           // {B, T, max_len, has_mask}
   int* err;
+  int32_t* index_dump;        // [T, 4] or null: (word id, position, type id, mask) per token
 };
 cudaError_t launch_embed_ln(const EmbedParams& p, int grid, cudaStream_t stream, bool pdl = false);
 

@@ -118,6 +118,9 @@ __global__ void __launch_bounds__(kRowThreads) embed_ln_kernel(EmbedParams p) {
       id = (id < 0 || id >= kVocab) ? 0 : id;
       ty = (ty < 0 || ty >= kTypes) ? 0 : ty;
       pos = pos >= kMaxPos ? kMaxPos - 1 : pos;
+      if (p.index_dump)  // the rows this token gathers, and whether it attends / is pooled
+        *reinterpret_cast<int4*>(p.index_dump + 4 * static_cast<size_t>(t)) =
+            make_int4(id, pos, ty, p.mask ? int(__ldg(p.mask + t) != 0) : 1);
     }
     const int n = min(chunk, p.total - base);
     for (int k = 0; k < n; k += 2) {

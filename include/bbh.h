@@ -81,20 +81,20 @@ BBH_API int bbh_weights_layers(const bbh_weights* w);
  * BBH_ERR_CAPACITY instead of overflowing. One workspace per concurrent stream. */
 BBH_API int bbh_ws_create(const bbh_weights* w, int max_tokens, int max_batch, int max_len, bbh_ws** out);
 BBH_API void bbh_ws_free(bbh_ws* ws);
-/* 1: the feed-forward block of every layer runs as one fused kernel (FFN1, GELU, FFN2,
- * residual LayerNorm; the intermediate stays on chip); 0 (default): two GEMM launches
- * through an HBM intermediate, as the reference's ffn_block -- currently the faster of the
- * two on B200 (the fused kernel's 128-wide 1-SM tiles use the tensor cores less well). */
-BBH_API int bbh_ws_set_ffn_fusion(bbh_ws* ws, int enable);
 /* 1 (default): the forward's kernels launch with programmatic dependent launch -- each
  * kernel lets the next one start its launch and prologue (barrier set-up, tensor-memory
  * allocation, weight staging) while it finishes, and the next one waits for its results
  * before touching them; 0: plain stream order. Results are identical either way. */
 BBH_API int bbh_ws_set_pdl(bbh_ws* ws, int enable);
-/* Tile shape of the bias and GELU projections (QKV, first FFN layer) in plans built after
- * the call (workspaces created and unit operations called later): 0 = one SM per 128-row
- * tile; 1 (default) = pairs of SMs sharing one 256-row tile (tcgen05 cta_group::2),
- * 192 columns wide where N allows, else 256; 2 = pairs, 256 columns first. Process-wide. */
+/* GEMM tile shape: 0 = one SM per 128-row tile; 1 (default) = pairs of SMs sharing one
+ * 256-row tile (tcgen05 cta_group::2), 192 columns wide where N allows, else 256; 2 = pairs,
+ * 256 columns first. Modes 0 and 1 give bit-identical results.
+ * bbh_ws_set_gemm_pairs sets it for one workspace (its plans are rebuilt by the next
+ * forward; not while a forward of that workspace is being enqueued on another thread).
+ * bbh_set_gemm_pairs sets the process-wide default (an atomic value) that workspaces
+ * created afterwards and the unit operators (bbh_linear*) use. No reference counterpart:
+ * the reference has one wmma tile shape (src/kernels/matmul.cu:64-92). */
+BBH_API int bbh_ws_set_gemm_pairs(bbh_ws* ws, int mode);
 BBH_API int bbh_set_gemm_pairs(int mode);
 /* 1 (default): bbh_embed* replay one captured CUDA graph per workspace; 0: eager launches. */
 BBH_API int bbh_ws_set_graph(bbh_ws* ws, int enable);
@@ -108,8 +108,8 @@ BBH_API int bbh_launches_per_forward(const bbh_ws* ws);
  * bbh_ws_kernel_times synchronises, adds the elapsed milliseconds and launch counts per
  * kernel kind into ms[BBH_KERNEL_KINDS] / counts[BBH_KERNEL_KINDS] and resets them.
  * Kinds: 0 embed+LN, 1 QKV GEMM, 2 attention, 3 O GEMM+LN, 4 FFN1 GEMM+GELU,
- * 5 FFN2 GEMM+LN, 6 pool+L2, 7 fused FFN block (4 and 5 only without fusion). */
-#define BBH_KERNEL_KINDS 8
+ * 5 FFN2 GEMM+LN, 6 pool+L2. */
+#define BBH_KERNEL_KINDS 7
 BBH_API int bbh_ws_set_kernel_timing(bbh_ws* ws, int enable);
 BBH_API int bbh_ws_kernel_times(bbh_ws* ws, double* ms, int64_t* counts);
 
@@ -137,6 +137,18 @@ BBH_API int bbh_encode_varlen(bbh_ws* ws, const bbh_weights* w, const int32_t* i
                       const int32_t* cu_seqlens, int batch, int total_tokens, int max_len, uint16_t* out,
                       uint16_t* layer_dump, void* stream);
 
+/* Parity aid: runs only the forward's first kernel (embedding gather + LayerNorm) and writes,
+ * per token t, indices[4t .. 4t+3] = (word id, position id, type id, mask) -- the rows the
+ * gather reads and whether the token attends / is pooled -- so a test can compare them with
+ * the reference's indexing for equality (src/kernels/embedding.cu:20-25: position = row %
+ * seq in the padded layout; src/kernels/pooling.cu:23-28: pooled where mask != 0). Packed
+ * when cu_seqlens is non-null (batch, total_tokens, max_len as bbh_embed_varlen; positions
+ * restart at 0 in each sentence), else padded (batch, seq, mask as bbh_embed). indices:
+ * device int32 [T, 4], 16-byte aligned. */
+BBH_API int bbh_embed_gather_indices(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
+                                     const int32_t* mask, const int32_t* cu_seqlens, int batch, int seq,
+                                     int total_tokens, int max_len, int32_t* indices, void* stream);
+
 /* ---- unit operators (the reference's launch_* kernel API) ---------------------------- */
 /* launch_matmul (src/kernels/matmul.h): C[M,N] = A[M,K] W[N,K]^T (+ bias) (+ erf-GELU).
  * N, K multiples of 8; 16-byte aligned pointers. */
@@ -147,12 +159,6 @@ BBH_API int bbh_linear(const uint16_t* A, const uint16_t* W, const uint16_t* bia
 BBH_API int bbh_linear_residual_layernorm(const uint16_t* A, const uint16_t* W, const uint16_t* bias,
                                   const uint16_t* residual, const uint16_t* gamma, const uint16_t* beta, float eps,
                                   uint16_t* C, int M, int K, void* stream);
-/* ffn_block (src/model/encoder.cu:52-64) as one kernel: out = LN(GELU(Y W1^T + b1) W2^T + b2
- * + Y) * gamma + beta; Y/out [M, 384], W1 [1536, 384], W2 [384, 1536] (nn.Linear
- * layouts); 16-byte aligned. */
-BBH_API int bbh_ffn_block(const uint16_t* Y, const uint16_t* W1, const uint16_t* b1, const uint16_t* W2,
-                          const uint16_t* b2, const uint16_t* gamma, const uint16_t* beta, float eps, uint16_t* out,
-                          int M, void* stream);
 /* launch_layernorm (src/kernels/layernorm.h): y = LN(x [+ residual]); D must be 384. */
 BBH_API int bbh_layernorm(const uint16_t* x, const uint16_t* gamma, const uint16_t* beta, uint16_t* y, int M, int D,
                   float eps, const uint16_t* residual, void* stream);
@@ -197,6 +203,16 @@ BBH_API int bbh_ws_set_corpus_lanes(bbh_ws* ws, int lanes);
 BBH_API int bbh_embed_corpus(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
                              const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
                              const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb, void* stream);
+/* bbh_embed_corpus_device: the same loop with the embeddings left in DEVICE memory for a
+ * collective to gather: emb_dev [m, 384] fp16 (16-byte aligned) receives the m sentences of
+ * this rank's batches in plan order (batch after batch, each batch's sentences in
+ * order[batch_first[b] .. batch_first[b+1])), so rank r's rows map to corpus rows through
+ * the plan. No device->host copy. Returns when every result is in emb_dev. Replaces the
+ * per-batch bert_embed loop of bench/corpus.cu:118-128 for a multi-GPU caller. */
+BBH_API int bbh_embed_corpus_device(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
+                                    const int64_t* offsets, int n, const int32_t* order, const int32_t* batch_first,
+                                    const int32_t* batch_rank, int n_batches, int rank, uint16_t* emb_dev,
+                                    void* stream);
 
 /* bbh_embed_padded: bert_embed (the call the reference's bench/bench.cu:44-49 repeats on
  * device-resident inputs) over consecutive batches of a padded [n, seq] corpus held in host
@@ -248,7 +264,8 @@ BBH_API int bbh_spearman(const float* x, const float* y, int n, double* rho);
  * max_len <= 512; larger requests return BBH_ERR_CAPACITY with a message saying so.
  * The first call on each device looks up the array's device address (a
  * cudaGetSymbolAddress with that device current), so make that first call before any
- * stream capture. All calls share the one array and it keeps the last call's contents:
+ * stream capture. The GEMM tensor maps are encoded on the host on the first call with a
+ * given weight set and reused while later calls pass the same one. All calls share the one array and it keeps the last call's contents:
  * calls that overlap on the GPU (for example on two streams of the same device) race and
  * corrupt each other's results, so serialise them. Device-side input errors go to the
  * array's own error word, cleared at the start of each call; read it with

@@ -249,6 +249,25 @@ class Oracle:
         return emb, packed
 
 
+def gather_indices(ids, types, mask=None, cu_seqlens=None) -> np.ndarray:
+    """(word id, position id, type id, mask) per token as the reference's embedding and
+    pooling kernels index them: padded [B, S] inputs use position = row % S
+    (src/kernels/embedding.cu:20-25) and pool where mask != 0 (src/kernels/pooling.cu:23-28);
+    a packed sentence is the same sentence padded on its own, so its positions restart at 0
+    and every token is real. Returns int32 [T, 4] in the input's token order."""
+    ids = np.asarray(ids)
+    types = np.zeros_like(ids) if types is None else np.asarray(types)
+    if cu_seqlens is not None:
+        cu = np.asarray(cu_seqlens, np.int64)
+        pos = np.concatenate([np.arange(cu[b + 1] - cu[b]) for b in range(len(cu) - 1)]) if len(cu) > 1 else []
+        m = np.ones(ids.size, np.int64)
+        return np.stack([ids.reshape(-1), np.asarray(pos, np.int64), types.reshape(-1), m], 1).astype(np.int32)
+    B, S = ids.shape
+    m = np.ones((B, S), np.int64) if mask is None else (np.asarray(mask) != 0).astype(np.int64)
+    pos = np.broadcast_to(np.arange(S), (B, S))
+    return np.stack([ids.reshape(-1), pos.reshape(-1), types.reshape(-1), m.reshape(-1)], 1).astype(np.int32)
+
+
 # --- synthetic inputs (stand-ins for the reference's tokenised STS sentences) ----------
 
 def sentence_ids(rng, length: int) -> np.ndarray:

@@ -7,8 +7,10 @@
 // into the directory that holds "weights/".
 #include <unistd.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
+#include <numeric>
 #include <string>
 #include <vector>
 
@@ -68,6 +70,81 @@ int ref_embed(const char* root, const int32_t* ids, const int32_t* types, const 
     cudaEventDestroy(b);
   }
   de.to_host(emb_host, size_t(batch) * model::HIDDEN * 2);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// The reference's dynamic-length corpus loop (bench/corpus.cu:80-128): sentences sorted by
+// length, cut into batches of B, each padded to its longest sentence rounded up to 16 (at
+// least 16), all batches resident on the device, one bert_embed per batch. Sentences come
+// packed (ids [cu[n]], cu [n+1]); each must be <= 128 tokens (the reference's SEQ_LEN).
+// Times `iters` passes over the corpus with CUDA events after one untimed pass and writes
+// ms per pass; emb_host (optional, [n, 384] fp16 bits) receives the embeddings in corpus
+// order.
+int ref_corpus(const char* root, const int32_t* ids, const int32_t* cu, int n, int B, int iters,
+               float* ms_per_pass, uint16_t* emb_host) {
+  if (n <= 0 || B <= 0) return -1;
+  for (int i = 0; i < n; ++i)
+    if (cu[i + 1] - cu[i] < 1 || cu[i + 1] - cu[i] > model::SEQ_LEN) return -1;
+  Cwd cd(root);
+  ModelWeights w = load_model_weights();
+  Workspace ws = make_workspace(B);
+  std::vector<int> order(n);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int a, int b) { return cu[a + 1] - cu[a] < cu[b + 1] - cu[b]; });
+  struct Batch {
+    DeviceBuffer ids, types, mask;
+    int size, eff, start;
+  };
+  std::vector<Batch> batches;
+  for (int s = 0; s < n; s += B) {
+    const int bs = std::min(B, n - s);
+    int mx = 0;
+    for (int k = 0; k < bs; ++k) mx = std::max(mx, cu[order[s + k] + 1] - cu[order[s + k]]);
+    const int eff = std::max(16, (mx + 15) / 16 * 16);
+    std::vector<int32_t> hi(size_t(bs) * eff, 0), ht(size_t(bs) * eff, 0), hm(size_t(bs) * eff, 0);
+    for (int k = 0; k < bs; ++k) {
+      const int si = order[s + k], L = cu[si + 1] - cu[si];
+      for (int j = 0; j < L; ++j) {
+        hi[size_t(k) * eff + j] = ids[cu[si] + j];
+        hm[size_t(k) * eff + j] = 1;
+      }
+    }
+    Batch b{DeviceBuffer(hi.size() * 4), DeviceBuffer(ht.size() * 4), DeviceBuffer(hm.size() * 4), bs, eff, s};
+    b.ids.from_host(hi.data(), hi.size() * 4);
+    b.types.from_host(ht.data(), ht.size() * 4);
+    b.mask.from_host(hm.data(), hm.size() * 4);
+    batches.push_back(std::move(b));
+  }
+  DeviceBuffer de(size_t(n) * model::HIDDEN * 2);
+  auto* ep = static_cast<__half*>(de.data());
+  auto pass = [&]() {
+    for (auto& b : batches)
+      bert_embed(ws, w, static_cast<const int32_t*>(b.ids.data()), static_cast<const int32_t*>(b.types.data()),
+                 static_cast<const int32_t*>(b.mask.data()), ep + size_t(b.start) * model::HIDDEN, b.size, b.eff);
+  };
+  pass();
+  if (iters > 0 && ms_per_pass) {
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a);
+    for (int i = 0; i < iters; ++i) pass();
+    cudaEventRecord(b);
+    cudaEventSynchronize(b);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a, b);
+    *ms_per_pass = ms / iters;
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+  }
+  if (emb_host) {
+    std::vector<uint16_t> h(size_t(n) * model::HIDDEN);
+    de.to_host(h.data(), h.size() * 2);
+    for (int i = 0; i < n; ++i)
+      std::memcpy(emb_host + size_t(order[i]) * model::HIDDEN, h.data() + size_t(i) * model::HIDDEN,
+                  model::HIDDEN * 2);
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

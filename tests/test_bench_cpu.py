@@ -33,3 +33,32 @@ def test_reference_arm_line():
 
 def test_reference_arm_other_ranks_silent():
     assert run_ref({"RANK": "1"}) == []
+
+
+def test_roofline_traffic_is_per_launch():
+    """roofline.traffic = ncu DRAM bytes per token x the tokens ONE launch processes: a layer
+    kernel runs once per layer of each forward, so a pass of F forwards over T tokens has
+    F x layers launches of T / F tokens each."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    T, layers, forwards, bpt = 8_900_000, 6, 128, 4390.5
+    per_launch = bench.traffic_per_launch("ffn2_gemm_ln", bpt, T, layers, forwards * layers)
+    assert abs(per_launch - bpt * T / forwards) <= 0.1 * bpt * T / forwards
+    # once-per-forward kernels
+    assert bench.traffic_per_launch("pool_l2", 769.4, T, layers, forwards) == 769.4 * T / forwards
+
+
+def test_kernel_entry_rooflines():
+    """A GEMM's roofline is the larger of its tensor time and its HBM time at the measured
+    peaks; the O projection (K = 384) is HBM-bound, FFN2 (K = 1536) tensor-bound."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    peaks = (6451.2, 1686.2, 1426.8)
+    T, layers, launches = 70_000 * 128, 6, 128 * 6
+    o = bench.kernel_entry("o_gemm_ln", 50e-3 * launches, launches, T, layers, 0.0, peaks)
+    f = bench.kernel_entry("ffn2_gemm_ln", 100e-3 * launches, launches, T, layers, 0.0, peaks)
+    assert o["bound"] == "hbm" and f["bound"] == "tensor"
+    assert abs(f["tflops"] - 2 * 70_000 * 384 * 1536 / 100e-6 / 1e12) < 1.0
+    assert f["roofline_frac"] == f["tensor_frac"] and o["roofline_frac"] == o["hbm_frac"]

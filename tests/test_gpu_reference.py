@@ -67,7 +67,7 @@ def ref_cuda(weights_root, ids, types, mask):
     return out.astype(np.float32)
 
 
-@pytest.mark.parametrize("batch,real,seq", [(64, 9, 16), (8, 9, 128), (16, 40, 64)])
+@pytest.mark.parametrize("batch,real,seq", [(64, 9, 16), (64, 9, 128), (16, 40, 64), (8, 128, 128)])
 def test_matches_reference_cuda(weights_root, batch, real, seq):
     ids, types, mask = om.padded_batch(batch, real, seq, seed=1)
     r = ref_cuda(weights_root, ids, types, mask)
@@ -78,6 +78,30 @@ def test_matches_reference_cuda(weights_root, batch, real, seq):
           f"cos(ref-cuda, torch) min {cos_rows(r, t).min():.6f}; cos(ours, torch) min {cos_rows(o, t).min():.6f}")
     assert c_ref.min() >= 0.999
     assert cos_rows(o, t).min() >= 0.9999
+
+
+def test_corpus_loop_matches_reference_cuda(weights_root):
+    """The reference's dynamic-length corpus loop (bench/corpus.cu:80-128: length-sorted
+    batches of 64, each padded to its longest rounded to 16) over a configs[2]-style corpus,
+    against bbh_embed_corpus on the same sentences (packed, token-bounded batches)."""
+    import bbh
+
+    if not os.path.exists(REF_LIB):
+        pytest.skip("oracle/_ref/libbbh_ref.so not built")
+    lens, rng = om.lognormal_lengths(700, seed=2)
+    ids, types, cu = om.packed_corpus(lens, rng)
+    L = ctypes.CDLL(REF_LIB)
+    ref = np.zeros((lens.size, 384), np.float16)
+    p = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    ids32, cu32 = np.ascontiguousarray(ids, np.int32), np.ascontiguousarray(cu, np.int32)
+    assert L.ref_corpus(weights_root.encode(), p(ids32), p(cu32), int(lens.size), 64, 0, None, p(ref)) == 0
+    gw = bbh.ModelWeights.load(os.path.join(weights_root, "weights"), 6, 0)
+    ws = bbh.Workspace(gw, 64 * 64, 64, 64)
+    plan = bbh.plan_batches(lens, 64, 64 * 64, 1)
+    ours_emb = ws.embed_corpus(ids, types, cu.astype(np.int64), plan)
+    c = cos_rows(ours_emb.astype(np.float32), ref.astype(np.float32))
+    print(f"corpus loop: cos(ours, ref-cuda) min {c.min():.6f}")
+    assert c.min() >= 0.999
 
 
 def test_cpp_dropin_example(weights_root, tmp_path):
