@@ -379,6 +379,9 @@ def measure(ctx, workload, n_per_gpu, steps, warmup, e2e_steps, gather=True, clo
     ws = bbh.Workspace(gw, max_tokens, batch, max_len)
     lanes = [ws] + [bbh.Workspace(gw, max_tokens, batch, max_len) for _ in range(args.lanes - 1)]
     ws.set_corpus_lanes(args.lanes)
+    if args.l2_persist:
+        for lw in lanes:
+            lw.set_l2_persist(True)
 
     gathered = None
     if packed:
@@ -549,6 +552,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--lanes", type=int, default=2, choices=[1, 2],
                     help="compute lanes: alternate batches over this many workspaces / streams")
+    ap.add_argument("--l2-persist", type=int, default=0, choices=[0, 1],
+                    help="1: forward launches carry a persisting L2 access-policy window over the layer weights")
     ap.add_argument("--gemm-pairs", type=int, default=1, choices=[0, 1, 2],
                     help="GEMM tiles: 0 = one SM per 128-row tile, 1 = SM pairs 256x192 (default), "
                          "2 = SM pairs 256x256 where N allows")
@@ -616,6 +621,7 @@ def main():
                 "l2": "inputs larger than L2 (each step streams ~1 GB of activations per GPU)",
                 "graph": "one CUDA graph per workspace, re-pointed per batch",
                 "lanes": f"{args.lanes} (batches alternate over {args.lanes} workspaces / streams)",
+                "l2_persist": bool(args.l2_persist),
                 "gemm_tiles": ["one SM per 128-row tile", "SM pairs, 256x192", "SM pairs, 256x256 where N allows"][args.gemm_pairs],
             },
             "roofline": roofline_of(res, layers),

@@ -46,6 +46,7 @@ _SIGS = {
     "bbh_ws_free": (None, [_P]),
     "bbh_ws_set_graph": (_I, [_P, _I]),
     "bbh_ws_set_gemm_pairs": (_I, [_P, _I]),
+    "bbh_ws_set_l2_persist": (_I, [_P, _I]),
     "bbh_ws_set_pdl": (_I, [_P, _I]),
     "bbh_set_gemm_pairs": (_I, [_I]),
     "bbh_device_error": (_I, [_P, _I]),
@@ -215,6 +216,10 @@ class Workspace:
         """GEMM tiles of this workspace's forwards: 0 = one SM per 128-row tile, 1 = SM pairs
         (256 x 192 where N allows, else 256 x 256), 2 = SM pairs, 256 x 256 first."""
         _check(lib().bbh_ws_set_gemm_pairs(self.handle, int(mode)))
+
+    def set_l2_persist(self, enable: bool):
+        """Forward launches carry an L2 access-policy window over the layer weights (persisting)."""
+        _check(lib().bbh_ws_set_l2_persist(self.handle, 1 if enable else 0))
 
     def set_kernel_timing(self, enable: bool):
         _check(lib().bbh_ws_set_kernel_timing(self.handle, 1 if enable else 0))

@@ -290,6 +290,9 @@ struct bbh_ws {
   int* err = nullptr;
   std::vector<GemmPlan> plans;  // 4 per layer: QKV, O+LN, FFN1+GELU, FFN2+LN
   int gemm_pairs = 1;           // make_gemm_plan's pair_mode for this workspace's plans
+  bool plans_stale = false;     // the plans must be rebuilt (tile mode changed)
+  bool l2_persist = false;      // forward launches carry an L2 access-policy window over the layer weights
+  cudaAccessPolicyWindow l2_window{};
   bool pdl = true;                      // programmatic dependent launch between the forward's kernels
   bool use_graph = true;
   cudaStream_t cap_stream = nullptr;
@@ -310,7 +313,16 @@ struct bbh_ws {
   int corpus_lanes = 1;
 };
 
+namespace {
+void drop_graph(bbh_ws* ws);
+}
+
 namespace bbh {
+namespace {
+thread_local const cudaAccessPolicyWindow* t_l2_window = nullptr;
+}
+const cudaAccessPolicyWindow* current_l2_window() { return t_l2_window; }
+void set_current_l2_window(const cudaAccessPolicyWindow* w) { t_l2_window = w; }
 int internal_fail(int code, const std::string& msg) { return fail(code, msg); }
 void ws_limits(const bbh_ws* ws, int* device, int* max_tokens, int* max_batch, int* max_len) {
   *device = ws->device;
@@ -323,6 +335,18 @@ void** ws_corpus_stage(bbh_ws* ws, void (*free_fn)(void*)) {
   return &ws->corpus_stage;
 }
 int ws_corpus_lanes(const bbh_ws* ws) { return ws->corpus_lanes; }
+void ws_inherit_settings(bbh_ws* dst, const bbh_ws* src) {
+  if (dst->pdl != src->pdl || dst->use_graph != src->use_graph || dst->gemm_pairs != src->gemm_pairs ||
+      dst->l2_persist != src->l2_persist || std::memcmp(&dst->l2_window, &src->l2_window, sizeof(dst->l2_window))) {
+    drop_graph(dst);
+    if (dst->gemm_pairs != src->gemm_pairs) dst->plans_stale = true;  // rebuilt with src's tiles
+    dst->pdl = src->pdl;
+    dst->use_graph = src->use_graph;
+    dst->gemm_pairs = src->gemm_pairs;
+    dst->l2_persist = src->l2_persist;
+    dst->l2_window = src->l2_window;
+  }
+}
 }  // namespace bbh
 
 namespace {
@@ -399,8 +423,21 @@ struct KernelMark {
 
 // Enqueue one forward. pool == false stops after the last layer (encode). dump, when
 // non-null, receives (layers+1) snapshots of the hidden state (eager mode only).
-int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh::PoolParams& pp,
-                    __half* dump, int total, cudaStream_t s) {
+int enqueue_forward_launches(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh::PoolParams& pp,
+                             __half* dump, int total, cudaStream_t s);
+
+// The forward's launches, with the workspace's L2 window (if any) on each of them.
+int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh::PoolParams& pp, __half* dump,
+                    int total, cudaStream_t s) {
+  struct WindowScope {
+    explicit WindowScope(const cudaAccessPolicyWindow* w) { bbh::set_current_l2_window(w); }
+    ~WindowScope() { bbh::set_current_l2_window(nullptr); }
+  } scope(ws->l2_persist ? &ws->l2_window : nullptr);
+  return enqueue_forward_launches(ws, ep, pool, pp, dump, total, s);
+}
+
+int enqueue_forward_launches(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh::PoolParams& pp,
+                             __half* dump, int total, cudaStream_t s) {
   using namespace bbh;
   const int L = ws->w->layers;
   const int row_grid = ws->num_sms * 8;
@@ -443,7 +480,7 @@ int enqueue_forward(bbh_ws* ws, const bbh::EmbedParams& ep, bool pool, const bbh
     if (dump) BBH_CUDA(cudaMemcpyAsync(dump + plane * (l + 1), ws->X, plane * 2, cudaMemcpyDeviceToDevice, s));
   }
   if (pool) {
-    int grid = ws->max_batch < ws->num_sms * 8 ? ws->max_batch : ws->num_sms * 8;
+    int grid = ws->max_batch < ws->num_sms * 16 ? ws->max_batch : ws->num_sms * 16;
     KernelMark km(ws, s, 6);
     BBH_CUDA(launch_pool_l2(pp, grid, s, ws->pdl));
   }
@@ -515,10 +552,11 @@ int prepare(bbh_ws* ws, const bbh_weights* w) {
   if (!ws || !w) return fail(BBH_ERR_ARG, "null workspace or weights");
   if (w->device != ws->device) return fail(BBH_ERR_ARG, "weights and workspace are on different devices");
   BBH_CUDA(cudaSetDevice(ws->device));
-  if (ws->w != w) {
+  if (ws->w != w || ws->plans_stale) {
     drop_graph(ws);
     int rc = build_plans(ws, w);
     if (rc) return rc;
+    ws->plans_stale = false;
   }
   return BBH_OK;
 }
@@ -549,8 +587,11 @@ bbh::PoolParams base_pool_params(bbh_ws* ws, uint16_t* emb) {
   return pp;
 }
 
+bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; }
+
 int check_padded(bbh_ws* ws, const int32_t* ids, const void* out, int batch, int seq) {
   if (!ids || !out) return fail(BBH_ERR_ARG, "null ids or output pointer");
+  if (misaligned16(out)) return fail(BBH_ERR_ARG, "the output must be 16-byte aligned");
   if (batch <= 0 || seq <= 0) return fail(BBH_ERR_ARG, "batch and seq must be positive");
   if (seq > BBH_MAX_POSITIONS) return fail(BBH_ERR_ARG, "seq exceeds the 512-entry position table");
   if (batch > ws->max_batch || seq > ws->max_len || int64_t(batch) * seq > ws->max_tokens)
@@ -561,6 +602,7 @@ int check_padded(bbh_ws* ws, const int32_t* ids, const void* out, int batch, int
 int check_packed(bbh_ws* ws, const int32_t* ids, const int32_t* cu, const void* out, int batch, int total,
                  int max_len) {
   if (!ids || !cu || !out) return fail(BBH_ERR_ARG, "null ids, cu_seqlens or output pointer");
+  if (misaligned16(out)) return fail(BBH_ERR_ARG, "the output must be 16-byte aligned");
   if (batch <= 0 || total < 0 || max_len <= 0) return fail(BBH_ERR_ARG, "bad batch / total_tokens / max_len");
   if (max_len > BBH_MAX_POSITIONS) return fail(BBH_ERR_ARG, "max_len exceeds the 512-entry position table");
   if (batch > ws->max_batch || total > ws->max_tokens || max_len > ws->max_len)
@@ -659,8 +701,41 @@ int bbh_ws_set_gemm_pairs(bbh_ws* ws, int mode) {
   if (mode != ws->gemm_pairs) {
     ws->gemm_pairs = mode;
     drop_graph(ws);
-    ws->w = nullptr;  // the plans are rebuilt with the new tiles by the next forward
+    ws->plans_stale = true;  // the plans are rebuilt with the new tiles by the next forward
   }
+  return BBH_OK;
+}
+
+int bbh_ws_set_l2_persist(bbh_ws* ws, int enable) {
+  if (!ws) return fail(BBH_ERR_ARG, "null workspace");
+  if (!enable) {
+    if (ws->l2_persist) drop_graph(ws);
+    ws->l2_persist = false;
+    return BBH_OK;
+  }
+  if (!ws->w) return fail(BBH_ERR_ARG, "bbh_ws_set_l2_persist: the workspace has no weights yet");
+  BBH_CUDA(cudaSetDevice(ws->device));
+  int max_persist = 0, max_window = 0;
+  BBH_CUDA(cudaDeviceGetAttribute(&max_persist, cudaDevAttrMaxPersistingL2CacheSize, ws->device));
+  BBH_CUDA(cudaDeviceGetAttribute(&max_window, cudaDevAttrMaxAccessPolicyWindowSize, ws->device));
+  if (max_persist <= 0 || max_window <= 0) return fail(BBH_ERR_UNSUPPORTED, "no persisting L2 on this device");
+  // the encoder layers' weights: from the first layer's QKV weight to the end of the arena
+  const bbh_weights* w = ws->w;
+  const __half* lo = w->L.front().qkv_w;
+  size_t bytes = size_t(w->arena + w->arena_elems - lo) * sizeof(__half);
+  if (bytes > size_t(max_window)) bytes = size_t(max_window);
+  size_t limit = 0;
+  BBH_CUDA(cudaDeviceGetLimit(&limit, cudaLimitPersistingL2CacheSize));
+  const size_t want = bytes < size_t(max_persist) ? bytes : size_t(max_persist);
+  // context-scoped: the set-aside ends with this process's CUDA context
+  if (limit < want) BBH_CUDA(cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, want));
+  ws->l2_window.base_ptr = const_cast<__half*>(lo);
+  ws->l2_window.num_bytes = bytes;
+  ws->l2_window.hitRatio = static_cast<float>(double(want) / double(bytes));
+  ws->l2_window.hitProp = cudaAccessPropertyPersisting;
+  ws->l2_window.missProp = cudaAccessPropertyStreaming;
+  ws->l2_persist = true;
+  drop_graph(ws);
   return BBH_OK;
 }
 
@@ -907,6 +982,8 @@ int bbh_attention_varlen(const uint16_t* qkv, uint16_t* ctx, const int32_t* cu_s
 int bbh_mean_pool_l2(const uint16_t* hidden, const int32_t* cu_seqlens, const uint8_t* tokmask, int batch,
                      uint16_t* emb, void* stream) {
   if (!hidden || !cu_seqlens || !emb || batch < 0) return fail(BBH_ERR_ARG, "bbh_mean_pool_l2: bad arguments");
+  if (misaligned16(hidden) || misaligned16(emb))
+    return fail(BBH_ERR_ARG, "bbh_mean_pool_l2: hidden and emb must be 16-byte aligned");
   int dev = 0;
   int rc = current_device(&dev);
   if (rc) return rc;
@@ -917,7 +994,7 @@ int bbh_mean_pool_l2(const uint16_t* hidden, const int32_t* cu_seqlens, const ui
   pp.meta = nullptr;
   pp.batch = batch;
   pp.emb = reinterpret_cast<__half*>(emb);
-  const int grid = batch < g_num_sms(dev) * 8 ? (batch > 0 ? batch : 1) : g_num_sms(dev) * 8;
+  const int grid = batch < g_num_sms(dev) * 16 ? (batch > 0 ? batch : 1) : g_num_sms(dev) * 16;
   BBH_CUDA(bbh::launch_pool_l2(pp, grid, static_cast<cudaStream_t>(stream)));
   return BBH_OK;
 }
@@ -1003,6 +1080,7 @@ int bbh_embed_varlen_static(const bbh_weights* w, const int32_t* ids, const int3
                             const int32_t* cu_seqlens, int batch, int total_tokens, int max_len, uint16_t* emb,
                             void* stream) {
   if (!w || !ids || !cu_seqlens || !emb) return fail(BBH_ERR_ARG, "bbh_embed_varlen_static: null pointer");
+  if (misaligned16(emb)) return fail(BBH_ERR_ARG, "bbh_embed_varlen_static: emb must be 16-byte aligned");
   if (batch <= 0 || total_tokens < 0 || max_len <= 0)
     return fail(BBH_ERR_ARG, "bbh_embed_varlen_static: bad batch / total_tokens / max_len");
   if (total_tokens > BBH_STATIC_MAX_TOKENS || batch > BBH_STATIC_MAX_BATCH || max_len > BBH_MAX_POSITIONS)

@@ -135,6 +135,7 @@ int acquire_stage(bbh_ws* ws, const bbh_weights* w, Stage** out, int* prev, cons
       rc = bbh::internal_fail(BBH_ERR_CUDA, std::string(who) + ": stream creation failed");
     if (rc) return rc;
   }
+  if (st.ws2) bbh::ws_inherit_settings(st.ws2, ws);
   *out = &st;
   return BBH_OK;
 }

@@ -11,13 +11,23 @@ struct bbh_ws;
 
 namespace bbh {
 
+// L2 access-policy window given to every launch of this thread while set (the forward's
+// launches when the workspace keeps its weights persisting in L2), or null.
+const cudaAccessPolicyWindow* current_l2_window();
+void set_current_l2_window(const cudaAccessPolicyWindow* w);
+
 // Launch with optional programmatic dependent launch (pdl) and cluster dimension.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
                       int cluster, Args... args) {
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[3];
   int na = 0;
+  if (const cudaAccessPolicyWindow* apw = current_l2_window()) {
+    attr[na].id = cudaLaunchAttributeAccessPolicyWindow;
+    attr[na].val.accessPolicyWindow = *apw;
+    ++na;
+  }
   if (pdl) {
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[na].val.programmaticStreamSerializationAllowed = 1;
@@ -49,6 +59,9 @@ void ws_limits(const bbh_ws* ws, int* device, int* max_tokens, int* max_batch, i
 void** ws_corpus_stage(bbh_ws* ws, void (*free_fn)(void*));
 // Number of compute lanes the corpus driver uses for this workspace (1 or 2).
 int ws_corpus_lanes(const bbh_ws* ws);
+// Gives dst (the corpus driver's second lane) src's launch settings: programmatic dependent
+// launch, graph use, GEMM tiles and the L2 window.
+void ws_inherit_settings(bbh_ws* dst, const bbh_ws* src);
 
 // ------------------------------------------------------------------ GEMM (tcgen05)
 enum Epilogue : int {

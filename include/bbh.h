@@ -96,6 +96,13 @@ BBH_API int bbh_ws_set_pdl(bbh_ws* ws, int enable);
  * the reference has one wmma tile shape (src/kernels/matmul.cu:64-92). */
 BBH_API int bbh_ws_set_gemm_pairs(bbh_ws* ws, int mode);
 BBH_API int bbh_set_gemm_pairs(int mode);
+/* 1: every kernel of this workspace's forwards carries an L2 access-policy window over the
+ * encoder layers' weights (hits persist, misses stream), and the process's persisting-L2
+ * set-aside is raised to the window's size (cudaLimitPersistingL2CacheSize; a setting of this
+ * process's CUDA context that ends with it). 0 (default): no window. Needs the weights the
+ * workspace was created with. The reference keeps its weights in 101 separate buffers with
+ * no cache policy (src/model/weights.h:86-107). */
+BBH_API int bbh_ws_set_l2_persist(bbh_ws* ws, int enable);
 /* 1 (default): bbh_embed* replay one captured CUDA graph per workspace; 0: eager launches. */
 BBH_API int bbh_ws_set_graph(bbh_ws* ws, int enable);
 /* Synchronises the device, returns the workspace's device error code (0 = none) and
@@ -116,7 +123,8 @@ BBH_API int bbh_ws_kernel_times(bbh_ws* ws, double* ms, int64_t* counts);
 /* ---- forward ------------------------------------------------------------------------
  * bert_embed (src/model/forward.h:17-19, forward.cu:44-53): ids/types/mask are
  * [batch, seq] int32 row-major (padded layout, position = row % seq); emb is
- * [batch, 384] fp16, unit L2 norm. types may be NULL (all 0), mask may be NULL (all 1).
+ * [batch, 384] fp16, unit L2 norm, 16-byte aligned (rows are written as 16-byte pieces;
+ * BBH_ERR_ARG otherwise). types may be NULL (all 0), mask may be NULL (all 1).
  * seq may be any value in [1, 512] (no multiple-of-16 requirement). */
 BBH_API int bbh_embed(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types, const int32_t* mask,
               uint16_t* emb, int batch, int seq, void* stream);
@@ -127,7 +135,7 @@ BBH_API int bbh_encode(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, con
 /* Packed variable-length form (no counterpart in the reference, which only pads):
  * ids/types are [total_tokens] (sentences back to back), cu_seqlens [batch+1] device
  * int32 offsets with cu_seqlens[0] = 0 and cu_seqlens[batch] = total_tokens; max_len
- * bounds every sentence length. emb is [batch, 384] fp16. */
+ * bounds every sentence length. emb is [batch, 384] fp16, 16-byte aligned. */
 BBH_API int bbh_embed_varlen(bbh_ws* ws, const bbh_weights* w, const int32_t* ids, const int32_t* types,
                      const int32_t* cu_seqlens, int batch, int total_tokens, int max_len, uint16_t* emb,
                      void* stream);
@@ -168,7 +176,8 @@ BBH_API int bbh_layernorm(const uint16_t* x, const uint16_t* gamma, const uint16
 BBH_API int bbh_attention_varlen(const uint16_t* qkv, uint16_t* ctx, const int32_t* cu_seqlens, const uint8_t* keymask,
                          int batch, int max_len, void* stream);
 /* launch_mean_pool + launch_l2_normalize (src/kernels/pooling.h, normalize.h) over
- * packed segments: hidden [T, 384] -> emb [batch, 384]; tokmask as above. */
+ * packed segments: hidden [T, 384] -> emb [batch, 384] (both 16-byte aligned); tokmask as
+ * above. */
 BBH_API int bbh_mean_pool_l2(const uint16_t* hidden, const int32_t* cu_seqlens, const uint8_t* tokmask, int batch,
                      uint16_t* emb, void* stream);
 

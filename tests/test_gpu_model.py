@@ -286,3 +286,38 @@ def test_all_attention_paths_vs_oracle(gw0, oracle0):
     ws1.set_gemm_pairs(0)
     got1 = embed_packed(ws1, ids, types, cu)
     assert np.array_equal(got.view(np.uint32), got1.view(np.uint32))
+
+
+def test_l2_window_and_tile_modes_bit_identical(gw0):
+    """The L2 access-policy window changes caching, not results; SM-pair and one-SM GEMM
+    tiles give the same bits; the corpus driver's second lane inherits the settings."""
+    import bbh
+    import synthetic as sy
+
+    lengths = sy.lengths_uniform(400, 8, 128, 11)
+    c = sy.bucketed_corpus(lengths, 400, 11)
+    b = c.batches[0]
+    d = lambda a: torch.as_tensor(np.asarray(a), dtype=torch.int32, device=DEV)
+    ids, types, cu = d(c.ids), d(c.types), d(b.cu)
+    outs = []
+    for persist, pairs in ((False, 1), (True, 1), (True, 0)):
+        ws = bbh.Workspace(gw0, b.tokens, 400, 128)
+        ws.set_gemm_pairs(pairs)
+        if persist:
+            ws.set_l2_persist(True)
+        for _ in range(2):
+            e = ws.embed_varlen(ids, types, cu, b.max_len)
+        outs.append(e.cpu().numpy().view(np.uint16))
+        assert ws.device_error() == 0
+    for o in outs[1:]:
+        assert np.array_equal(o, outs[0])
+    # the two-lane corpus driver with the window on equals the plain forward
+    ws = bbh.Workspace(gw0, b.tokens, 400, 128)
+    ws.set_corpus_lanes(2)
+    ws.set_l2_persist(True)
+    offsets = np.zeros(401, np.int64)
+    offsets[1:] = np.cumsum(lengths[c.order])
+    plan = bbh.plan_batches(np.diff(offsets).astype(np.int32), 100, b.tokens, 1)
+    got = ws.embed_corpus(c.ids, c.types, offsets, plan)
+    ref = embed_packed(bbh.Workspace(gw0, b.tokens, 400, 128), c.ids, c.types, b.cu)
+    assert cos_rows(got.astype(np.float32), ref).min() >= 0.99999
