@@ -19,7 +19,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-I" + os.path.join(HERE, "..", "include")]
-SOURCES = ["gemm_tc.cu", "gemm_pair.cu", "attention_tc.cu", "rowwise.cu", "capi.cu", "corpus.cu", "similarity.cu", "blob.cu", "tokenizer.cu"]
+SOURCES = ["gemm_tc.cu", "gemm_pair.cu", "gemm_ln.cu", "attention_tc.cu", "rowwise.cu", "capi.cu", "corpus.cu", "similarity.cu", "blob.cu", "tokenizer.cu"]
 
 
 def _needs(target: str, deps: list[str]) -> bool:

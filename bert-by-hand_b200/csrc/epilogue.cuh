@@ -74,6 +74,111 @@ __device__ __forceinline__ void epi_pack32(const float* v, int col0, const float
   }
 }
 
+// ---------------------------------------------------------------- residual LayerNorm pieces
+// Shared by every residual-LayerNorm epilogue (LnSlice below, gemm_ln.cu), so that all of
+// them compute bit-identical results. The arithmetic runs on packed fp32 pairs (sm_100's
+// f32x2 add / sub / mul / fma: two columns per instruction, each rounded as the scalar op).
+__device__ __forceinline__ unsigned long long f2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 f2_split(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2_sub(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// x = accumulator + (bias + residual) for 8 columns: acc[8] fp32, bias[8] fp32 (16-byte
+// aligned), res = 8 fp16 values; x as four packed pairs.
+__device__ __forceinline__ void ln_x8(const float* acc, const float* bias, uint4 res, unsigned long long (&x)[4]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&res);
+  const float4 b0 = *reinterpret_cast<const float4*>(bias);
+  const float4 b1 = *reinterpret_cast<const float4*>(bias + 4);
+  const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 r = __half22float2(h[e]);
+    x[e] = f2_add(f2(acc[2 * e], acc[2 * e + 1]), f2_add(f2(bb[2 * e], bb[2 * e + 1]), f2(r.x, r.y)));
+  }
+}
+
+// x = accumulator + (bias + residual) over 64 columns of one row, in place (v[64] holds the
+// fp32 accumulator on entry and x on return; bias[64], res[8] as for ln_x8), and the mean
+// and M2 (sum of squared deviations) of x, from sums shifted by the first x; even and odd
+// columns accumulate in the two halves of packed pairs and are added at the end.
+__device__ __forceinline__ void ln_stats64(float* v, const float* bias, const uint4* res, float& mean, float& m2) {
+  unsigned long long s1 = f2(0.f, 0.f), s2 = f2(0.f, 0.f), sh = 0;
+  float shift = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    unsigned long long x[4];
+    ln_x8(v + 8 * j, bias + 8 * j, res[j], x);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (j == 0 && e == 0) {
+        shift = f2_split(x[0]).x;
+        sh = f2(shift, shift);
+      }
+      const unsigned long long d = f2_sub(x[e], sh);
+      s1 = f2_add(s1, d);
+      s2 = f2_fma(d, d, s2);
+      const float2 xf = f2_split(x[e]);
+      v[8 * j + 2 * e] = xf.x;
+      v[8 * j + 2 * e + 1] = xf.y;
+    }
+  }
+  const float2 a = f2_split(s1), b = f2_split(s2);
+  const float t1 = a.x + a.y, t2 = b.x + b.y;
+  mean = shift + t1 * (1.0f / 64);
+  m2 = fmaxf(t2 - t1 * t1 * (1.0f / 64), 0.f);
+}
+
+// (x - mean) * rstd * gamma + beta for 64 columns of x starting at column col, packed fp16
+// into 8 16-byte pieces.
+__device__ __forceinline__ void ln_norm64(const float* x, const float* gamma, const float* beta, int col,
+                                          unsigned long long mean2, unsigned long long rstd2, uint4* out) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 g0 = *reinterpret_cast<const float4*>(gamma + col + 8 * j);
+    const float4 g1 = *reinterpret_cast<const float4*>(gamma + col + 8 * j + 4);
+    const float4 c0 = *reinterpret_cast<const float4*>(beta + col + 8 * j);
+    const float4 c1 = *reinterpret_cast<const float4*>(beta + col + 8 * j + 4);
+    const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const unsigned long long xe = f2(x[8 * j + 2 * e], x[8 * j + 2 * e + 1]);
+      const unsigned long long t = f2_mul(f2_sub(xe, mean2), rstd2);
+      const float2 o = f2_split(f2_fma(t, f2(gg[2 * e], gg[2 * e + 1]), f2(cc[2 * e], cc[2 * e + 1])));
+      w[e] = pack_half2(o.x, o.y);
+    }
+    out[j] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // Residual + bias + LayerNorm epilogue of one warp's 32-row x 64-column slice of an output
 // row block whose 384 columns are split over two CTAs of a cluster (192 columns each,
 // three 64-column warps per TMEM lane quadrant per CTA). Row statistics are combined in
@@ -117,24 +222,15 @@ struct LnSlice {
     uint4 res[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) res[j] = *reinterpret_cast<const uint4*>(rowp + ((j ^ sw) << 4));
-    add32(v, bias + c0, &res[0]);
-    add32(v + 32, bias + c0 + 32, &res[4]);
-    // shifted sums (shift = this lane's first value) -> part mean and M2
-    const float shift = v[0];
-    float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      const float d = v[j] - shift;
-      s1 += d;
-      s2 += d * d;
-    }
+    float pmean, pm2;
+    ln_stats64(v, bias + c0, res, pmean, pm2);
     // Two scratch slots alternate by tile, so one barrier per tile suffices: a warp can
     // rewrite a slot only after every part has passed the next tile's barrier.
     const int rloc = quad * 32 + lane;
     const int slot = iter & 1;
     float* rs = red + slot * (2 * kParts * 128);
-    rs[part * 128 + rloc] = shift + s1 * (1.0f / 64);
-    rs[kParts * 128 + part * 128 + rloc] = fmaxf(s2 - s1 * s1 * (1.0f / 64), 0.f);
+    rs[part * 128 + rloc] = pmean;
+    rs[kParts * 128 + part * 128 + rloc] = pm2;
     named_barrier(1 + quad, 32 * kParts);
     float mean_c = 0.f;
 #pragma unroll
@@ -161,12 +257,10 @@ struct LnSlice {
     const float m2 = m2_c + ps.y + dp * dp * (0.5f * 192);
     const float rstd = rsqrtf(m2 * (1.0f / kHidden) + eps);
     // normalise, affine, write the row back over its residual, store the slice
-    uint32_t w[32];
-    pack32(v, c0, mean, rstd, w);
-    pack32(v + 32, c0 + 32, mean, rstd, w + 16);
+    uint4 y[8];
+    ln_norm64(v, gamma, beta, c0, f2(mean, mean), f2(rstd, rstd), y);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      *reinterpret_cast<uint4*>(rowp + ((j ^ sw) << 4)) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+    for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(rowp + ((j ^ sw) << 4)) = y[j];
     fence_async_shared();
     __syncwarp();
     if (lane == 0) {
@@ -179,27 +273,6 @@ struct LnSlice {
       }
     }
     return true;
-  }
-
-  __device__ __forceinline__ static void add32(float* v, const float* b, const uint4* res4) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float r8[8];
-      unpack_half8(res4[j], r8);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[j * 8 + e] += b[j * 8 + e] + r8[e];
-    }
-  }
-
-  __device__ __forceinline__ void pack32(const float* v, int col0, float mean, float rstd, uint32_t* w) const {
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 g = *reinterpret_cast<const float4*>(gamma + col0 + 4 * q);
-      const float4 b = *reinterpret_cast<const float4*>(beta + col0 + 4 * q);
-      const float* x = v + 4 * q;
-      w[2 * q] = pack_half2((x[0] - mean) * rstd * g.x + b.x, (x[1] - mean) * rstd * g.y + b.y);
-      w[2 * q + 1] = pack_half2((x[2] - mean) * rstd * g.z + b.z, (x[3] - mean) * rstd * g.w + b.w);
-    }
   }
 };
 

@@ -1,19 +1,14 @@
-// CTA-pair (cta_group::2) tcgen05 GEMM for the encoder's four dense layers:
-//   C[rows, N] = A[rows, K] . W[N, K]^T + bias   (+ erf-GELU | + residual, LayerNorm)
-// i.e. the fused QKV projection (N = 1152), the first FFN layer (N = 1536, GELU) and the
-// two N = 384 projections with the residual LayerNorm: the reference's wmma GEMM
-// (src/kernels/matmul.cu:94-186) followed by its bias / GELU kernels and its residual
-// LayerNorm (src/kernels/layernorm.cu:17-59, called at src/model/encoder.cu:49-50, :63-64).
+// CTA-pair (cta_group::2) tcgen05 GEMM for the encoder's bias / GELU projections:
+//   C[rows, N] = A[rows, K] . W[N, K]^T + bias   (+ erf-GELU)
+// i.e. the fused QKV projection (N = 1152) and the first FFN layer (N = 1536, GELU): the
+// reference's wmma GEMM (src/kernels/matmul.cu:94-186) followed by its bias / GELU
+// kernels. The two N = 384 projections with the residual LayerNorm run on gemm_ln.cu.
 //
 // Why pairs: with one SM per 128 x BN tile every SM streams its own copy of the B tile
 // (BN x 64 per k-block) from L2 next to its A tile, and at full tensor rate that L2 ->
 // shared-memory traffic is the limit. Two SMs of a cluster working one 256 x BN tile with
 // one M=256 MMA each hold 128 A rows and only BN/2 B rows, so the operand bytes per FLOP
 // drop by 1.4x (BN=192) to 1.6x (BN=256) at the same accumulator size per SM.
-//
-// LayerNorm: a 4-CTA cluster holds two pairs, pair 0 columns 0-191 and pair 1 columns
-// 192-383 of the same 256 rows; CTA r and CTA r ^ 2 own the same 128 rows and exchange
-// per-row statistics through distributed shared memory (LnSlice, epilogue.cuh).
 //
 // Roles (both CTAs of a pair run every role except the MMA issue):
 //  * warp 0 lane 0: TMA producer for this CTA's halves (A rows, B rows) of each k-block;
@@ -32,8 +27,8 @@ namespace bbh {
 
 template <int BN, int PARTS, int EPI>
 struct PairCfg {
-  static constexpr bool LN = EPI == kEpiResLN;
-  static constexpr int CLUSTER = LN ? 4 : 2;
+  static_assert(EPI == kEpiBias || EPI == kEpiGelu, "bias / GELU epilogues");
+  static constexpr int CLUSTER = 2;
   static constexpr int BM = 128;           // accumulator rows per CTA (256 per pair)
   static constexpr int BK = 64;            // one 128-byte swizzle row of fp16
   static constexpr int B_ROWS = BN / 2;    // B rows held by each CTA
@@ -42,12 +37,9 @@ struct PairCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int EPI_WARPS = 4 * PARTS;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  static constexpr int STAGING_BYTES = EPI_WARPS * 4096;
-  static constexpr int BIAS_COLS = LN ? kHidden : kMaxBiasCols;
-  static constexpr int AUX_BYTES = 512 /*barriers*/ + 4 * BIAS_COLS +
-                                   (LN ? 8 * kHidden /*gamma, beta*/ + 2 * 2 * 3 * 128 * 4 /*row statistics*/ +
-                                             2048 /*partner statistics*/
-                                       : 0);
+  static constexpr int STAGING_BYTES = EPI_WARPS * 4096;  // per epilogue warp: 32 rows x 128 B
+  static constexpr int BIAS_COLS = kMaxBiasCols;
+  static constexpr int AUX_BYTES = 512 /*barriers*/ + 4 * BIAS_COLS;
   static constexpr int RING_BYTES = 227 * 1024 - 1024 - STAGING_BYTES - AUX_BYTES;
   static constexpr int STAGES = RING_BYTES / STAGE_BYTES > 8 ? 8 : RING_BYTES / STAGE_BYTES;
   static constexpr int NACC = 2;
@@ -58,13 +50,12 @@ struct PairCfg {
   static_assert(NACC * BN <= TMEM_COLS, "TMEM overflow");
   static_assert(STAGES >= 3, "operand ring too shallow");
   static_assert(SMEM <= 227 * 1024, "shared memory over the per-CTA limit");
-  static_assert(!LN || (BN == 192 && PARTS == 3), "LayerNorm: 256 x 192 pair tiles, 3 warps per quadrant");
 };
 
 template <int BN, int EPI, int PARTS>
 __global__ void __launch_bounds__(PairCfg<BN, PARTS, EPI>::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, GemmParams p) {
+                     const __grid_constant__ CUtensorMap tmC, GemmParams p) {
   using Cfg = PairCfg<BN, PARTS, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int NACC = Cfg::NACC;
@@ -80,23 +71,16 @@ __global__ void __launch_bounds__(PairCfg<BN, PARTS, EPI>::THREADS, 1)
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* accf_bar = empty_bar + STAGES;
   uint64_t* acce_bar = accf_bar + NACC;  // used in the even CTA
-  uint64_t* xfull_bar = acce_bar + NACC;  // [2] partner statistics arrived (LayerNorm)
-  uint64_t* res_bar = xfull_bar + 2;      // [EPI_WARPS] residual slice landed (LayerNorm)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(res_bar + Cfg::EPI_WARPS);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce_bar + NACC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* s_bias = reinterpret_cast<float*>(s_stage + Cfg::STAGING_BYTES + 512);  // [BIAS_COLS]
-  float* s_gamma = s_bias + Cfg::BIAS_COLS;                                        // [384]
-  float* s_beta = s_gamma + kHidden;                                               // [384]
-  float* red = s_beta + kHidden;                                 // [2][2][3][128] (LayerNorm)
-  float2* xstat = reinterpret_cast<float2*>(red + 2 * 2 * 3 * 128);  // [2][128] (LayerNorm)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t crank = cluster_ctarank();
   const uint32_t lead_rank = crank & ~1u;  // even CTA of this CTA's pair
   const bool leader = crank == lead_rank;
-  const int half = static_cast<int>(crank & 1);   // which 128 rows of the pair tile
-  const int pair = static_cast<int>(crank >> 1);  // LayerNorm: which 192 columns
+  const int half = static_cast<int>(crank & 1);  // which 128 rows of the pair tile
 
   pdl_launch_dependents();
   const int n_tiles = (p.N + BN - 1) / BN;
@@ -113,40 +97,29 @@ __global__ void __launch_bounds__(PairCfg<BN, PARTS, EPI>::THREADS, 1)
       mbar_init(&accf_bar[a], 1);
       mbar_init(&acce_bar[a], 2 * Cfg::EPI_WARPS);  // every epilogue warp of both CTAs
     }
-    // partner statistics: one local arrival (with the byte count) + 128 rows x 8 B
-    mbar_init(&xfull_bar[0], 1);
-    mbar_init(&xfull_bar[1], 1);
-    for (int w = 0; w < Cfg::EPI_WARPS; ++w) mbar_init(&res_bar[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmC);
-    if constexpr (Cfg::LN) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) tmem_alloc_pair(tmem_holder, Cfg::TMEM_COLS);
   const bool bias_in_smem = p.bias && p.N <= Cfg::BIAS_COLS;
   if (bias_in_smem)
     for (int i = threadIdx.x; i < p.N; i += blockDim.x) s_bias[i] = __half2float(p.bias[i]);
-  if constexpr (Cfg::LN) {
-    for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
-      s_gamma[i] = __half2float(p.gamma[i]);
-      s_beta[i] = __half2float(p.beta[i]);
-    }
-  }
   pdl_wait();
   const int rows = p.rows_dev ? *p.rows_dev : p.rows;
   const int m_pairs = (rows + 2 * Cfg::BM - 1) / (2 * Cfg::BM);
-  const int num_tiles = Cfg::LN ? m_pairs : m_pairs * n_tiles;
+  const int num_tiles = m_pairs * n_tiles;
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // every CTA's barriers initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   // tile t: rows [256 * m, +256) with this CTA's 128 at +128 * half; columns [n0, +BN),
-  // (m, n0) = (t / n_tiles, BN * (t % n_tiles)), or (t, BN * pair) for LayerNorm
-  auto tile_m0 = [&](int t) { return (Cfg::LN ? t : t / n_tiles) * (2 * Cfg::BM) + half * Cfg::BM; };
-  auto tile_n0 = [&](int t) { return Cfg::LN ? pair * BN : (t % n_tiles) * BN; };
+  // (m, n0) = (t / n_tiles, BN * (t % n_tiles))
+  auto tile_m0 = [&](int t) { return (t / n_tiles) * (2 * Cfg::BM) + half * Cfg::BM; };
+  auto tile_n0 = [&](int t) { return (t % n_tiles) * BN; };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -225,48 +198,28 @@ __global__ void __launch_bounds__(PairCfg<BN, PARTS, EPI>::THREADS, 1)
     ChunkStore cst{s_stage + we * 4096, &tmC, lane};
     const uint32_t acce0 = mapa_shared(smem_u32(acce_bar), lead_rank);
     const float* sb = bias_in_smem ? s_bias : nullptr;
-    // LayerNorm: the residual slice of the first tile is queued before the loop
-    const LnSlice ln{cst.buf, &tmC, &tmR, &res_bar[we], red, xstat, xfull_bar, crank ^ 2u,
-                     s_bias, s_gamma, s_beta, p.eps, lane, quad, part, we};
-    if constexpr (Cfg::LN) {
-      if (first_tile < num_tiles) ln.prefetch(tile_n0(first_tile) + part * HB, tile_m0(first_tile) + quad * 32);
-    }
     int acc = 0;
     uint32_t acc_phase = 0;
-    int iter = 0;  // tiles processed by this CTA (LayerNorm statistics slot and phase)
-    for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++iter) {
+    for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
       if (!mbar_wait(&accf_bar[acc], acc_phase, abort_flag, p.err)) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + lane_off + acc * BN + part * HB;
       const int row0 = tile_m0(tile) + quad * 32;
       const int c0 = tile_n0(tile) + part * HB;
-      if constexpr (Cfg::LN) {
-        float v[64];
-        tmem_ld64(tacc, tacc + 32, v);
-        // accumulator read by this warp: release it to the even CTA's MMA thread
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(acce0 + acc * 8);
-        const int nt = tile + tile_step;
-        if (!ln.finish(v, iter, c0, row0, nt < num_tiles, tile_n0(nt) + part * HB, tile_m0(nt) + quad * 32,
-                       abort_flag, p.err))
-          break;
-      } else {
 #pragma unroll 1
-        for (int c = 0; c < HB; c += 64) {
-          float v[64];
-          tmem_ld64(tacc + c, tacc + c + 32, v);
-          if (c + 64 >= HB) {
-            // accumulator fully read by this warp: release it to the even CTA's MMA thread
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acce0 + acc * 8);
-          }
-          uint32_t w[32];
-          epi_pack32<EPI>(v, c0 + c, sb, p.bias, p.N, w);
-          epi_pack32<EPI>(v + 32, c0 + c + 32, sb, p.bias, p.N, w + 16);
-          cst.put64(w, c0 + c, row0);
+      for (int c = 0; c < HB; c += 64) {
+        float v[64];
+        tmem_ld64(tacc + c, tacc + c + 32, v);
+        if (c + 64 >= HB) {
+          // accumulator fully read by this warp: release it to the even CTA's MMA thread
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(acce0 + acc * 8);
         }
+        uint32_t w[32];
+        epi_pack32<EPI>(v, c0 + c, sb, p.bias, p.N, w);
+        epi_pack32<EPI>(v + 32, c0 + c + 32, sb, p.bias, p.N, w + 16);
+        cst.put64(w, c0 + c, row0);
       }
       if (++acc == NACC) {
         acc = 0;
@@ -324,11 +277,11 @@ static cudaError_t launch_pair_inst(const GemmPlan& plan, cudaStream_t stream, b
     attr_set[dev] = true;
   }
   const int m_pairs = (plan.rows_cap + 255) / 256;
-  const int tiles_cap = Cfg::LN ? m_pairs : m_pairs * ((plan.p.N + BN - 1) / BN);
+  const int tiles_cap = m_pairs * ((plan.p.N + BN - 1) / BN);
   int nclusters = dev < 64 ? max_clusters[dev] : 64;
   if (nclusters > tiles_cap) nclusters = tiles_cap;
   return launch_ex(kern, dim3(Cfg::CLUSTER * nclusters), dim3(Cfg::THREADS), Cfg::SMEM, stream, pdl, Cfg::CLUSTER,
-                   plan.tmA, plan.tmB2, plan.tmC, plan.tmR, plan.p);
+                   plan.tmA, plan.tmB2, plan.tmC, plan.p);
 }
 
 bool gemm_pair_supported(int N, int epi, int bn) {
@@ -343,7 +296,7 @@ cudaError_t launch_gemm_pair(const GemmPlan& plan, cudaStream_t stream, bool pdl
     case kEpiGelu * 1000 + 192: return launch_pair_inst<192, kEpiGelu, 3>(plan, stream, pdl);
     case kEpiBias * 1000 + 256: return launch_pair_inst<256, kEpiBias, 4>(plan, stream, pdl);
     case kEpiGelu * 1000 + 256: return launch_pair_inst<256, kEpiGelu, 4>(plan, stream, pdl);
-    case kEpiResLN * 1000 + 192: return launch_pair_inst<192, kEpiResLN, 3>(plan, stream, pdl);
+    case kEpiResLN * 1000 + 192: return launch_gemm_ln_pair(plan, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

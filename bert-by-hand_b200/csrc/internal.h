@@ -117,6 +117,8 @@ cudaError_t launch_gemm(const GemmPlan& plan, cudaStream_t stream, bool pdl = fa
 // CTA-pair kernel (gemm_pair.cu): bias / GELU epilogues, N a multiple of the pair width.
 bool gemm_pair_supported(int N, int epi, int bn);
 cudaError_t launch_gemm_pair(const GemmPlan& plan, cudaStream_t stream, bool pdl);
+// CTA-pair residual-LayerNorm GEMM over whole 384-wide rows (gemm_ln.cu).
+cudaError_t launch_gemm_ln_pair(const GemmPlan& plan, cudaStream_t stream, bool pdl);
 // Process-wide default tile mode (make_gemm_plan's pair_mode) for the unit operators and
 // for workspaces created afterwards; a workspace keeps its own copy.
 int default_gemm_pair_mode();
