@@ -378,7 +378,7 @@ def measure(ctx, workload, n_per_gpu, steps, warmup, e2e_steps, gather=True, clo
         plan = None
     ws = bbh.Workspace(gw, max_tokens, batch, max_len)
     lanes = [ws] + [bbh.Workspace(gw, max_tokens, batch, max_len) for _ in range(args.lanes - 1)]
-    ws.set_corpus_lanes(args.lanes)
+    ws.set_corpus_lanes(min(args.lanes, 2))
     if args.l2_persist:
         for lw in lanes:
             lw.set_l2_persist(True)
@@ -550,8 +550,9 @@ def main():
     ap.add_argument("--no-side-runs", action="store_true", help="skip the other workloads' short runs")
     ap.add_argument("--no-reference-cuda", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--lanes", type=int, default=2, choices=[1, 2],
-                    help="compute lanes: alternate batches over this many workspaces / streams")
+    ap.add_argument("--lanes", type=int, default=2, choices=[1, 2, 3, 4],
+                    help="compute lanes: alternate batches over this many workspaces / streams (the e2e "
+                         "corpus driver uses at most 2)")
     ap.add_argument("--l2-persist", type=int, default=0, choices=[0, 1],
                     help="1: forward launches carry a persisting L2 access-policy window over the layer weights")
     ap.add_argument("--gemm-pairs", type=int, default=1, choices=[0, 1, 2],
