@@ -430,7 +430,11 @@ int make_gemm_plan(GemmPlan* plan, const __half* A, int lda, int rows_cap, const
   plan->bn = bn;
   plan->bn2 = 0;
   memset(&plan->tmB2, 0, sizeof(plan->tmB2));
-  if (pair_mode) {
+  // The residual-LayerNorm pair kernel gives each SM pair a whole 256-row tile; when a
+  // launch has fewer such tiles than SM pairs (small batches), the one-SM kernel's 128-row
+  // tiles on 2-CTA clusters keep more SMs busy (the two give bit-identical results).
+  const bool ln_small = epi == kEpiResLN && (rows_cap + 255) / 256 < num_sms / 2;
+  if (pair_mode && !ln_small) {
     const int order[2] = {pair_mode == 2 ? 256 : 192, pair_mode == 2 ? 192 : 256};
     for (int b2 : order)
       if (gemm_pair_supported(N, epi, b2)) {
