@@ -227,8 +227,10 @@ int corpus_run(const char* who, bbh_ws* ws, const bbh_weights* w, const int32_t*
     return bbh::internal_fail(BBH_ERR_ARG, name + ": batch_first must run from 0 to n");
   int device = 0, max_tokens = 0, max_batch = 0, max_len = 0;
   bbh::ws_limits(ws, &device, &max_tokens, &max_batch, &max_len);
-  // validate the whole plan on the host before anything is queued
+  // validate this rank's batches on the host before anything is queued (other ranks'
+  // batches may need more capacity than this rank's workspace has)
   for (int b = 0; b < n_batches; ++b) {
+    if (batch_rank[b] != rank) continue;
     const int lo = batch_first[b], hi = batch_first[b + 1];
     if (hi < lo || hi - lo > max_batch)
       return bbh::internal_fail(BBH_ERR_CAPACITY, name + ": batch " + std::to_string(b) +

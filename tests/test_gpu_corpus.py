@@ -82,6 +82,25 @@ def test_two_ranks_reassemble(setup):
     assert np.all(np.abs(norms - 1) < 2e-3)
 
 
+def test_rank_workspace_sized_for_its_own_batches(setup):
+    """A rank's workspace needs only its own batches' capacity: another rank's larger batches
+    are not this rank's to run (the multi-GPU bench sizes each rank's workspace this way);
+    host and device outputs agree with the one-rank run."""
+    bbh, w, gw, lengths, ids, types, offsets = setup
+    one = bbh.plan_batches(lengths, 128, 8192, 1)
+    two = bbh.plan_batches(lengths, 128, 8192, 2)
+    full = bbh.Workspace(gw, 8192, 128, 128).embed_corpus(ids, types, offsets, one)
+    for r in (0, 1):
+        mine = two.rank_order(r)
+        own_tokens = max(int(lengths[idx].sum()) for _, idx in two.batches(r))
+        own_len = max(int(lengths[idx].max()) for _, idx in two.batches(r))
+        ws = bbh.Workspace(gw, own_tokens, 128, own_len)
+        host = ws.embed_corpus(ids, types, offsets, two, rank=r)
+        dev = ws.embed_corpus_device(ids, types, offsets, two, rank=r)
+        assert np.array_equal(host[mine].view(np.uint16), full[mine].view(np.uint16))
+        assert np.array_equal(dev[:mine.size].cpu().numpy().view(np.uint16), full[mine].view(np.uint16))
+
+
 def test_capacity_checked_before_work(setup):
     bbh, w, gw, lengths, ids, types, offsets = setup
     ws = bbh.Workspace(gw, 1024, 32, 128)
