@@ -555,9 +555,9 @@ def main():
                          "corpus driver uses at most 2)")
     ap.add_argument("--l2-persist", type=int, default=0, choices=[0, 1],
                     help="1: forward launches carry a persisting L2 access-policy window over the layer weights")
-    ap.add_argument("--gemm-pairs", type=int, default=1, choices=[0, 1, 2],
-                    help="GEMM tiles: 0 = one SM per 128-row tile, 1 = SM pairs 256x192 (default), "
-                         "2 = SM pairs 256x256 where N allows")
+    ap.add_argument("--gemm-pairs", type=int, default=2, choices=[0, 1, 2],
+                    help="GEMM tiles: 0 = one SM per 128-row tile, 1 = SM pairs 256x192, "
+                         "2 = SM pairs 256x256 where N allows (default)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -623,7 +623,7 @@ def main():
                 "graph": "one CUDA graph per workspace, re-pointed per batch",
                 "lanes": f"{args.lanes} (batches alternate over {args.lanes} workspaces / streams)",
                 "l2_persist": bool(args.l2_persist),
-                "gemm_tiles": ["one SM per 128-row tile", "SM pairs, 256x192", "SM pairs, 256x256 where N allows"][args.gemm_pairs],
+                "gemm_tiles": ["one SM per 128-row tile", "SM pairs, 256x192", "SM pairs, 256x256 where N allows (FFN1), else 256x192; residual-LN GEMMs 256x384 per pair"][args.gemm_pairs],
             },
             "roofline": roofline_of(res, layers),
             "kernels": res["kernels"],

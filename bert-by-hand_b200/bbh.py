@@ -475,7 +475,8 @@ def spearman(x, y) -> float:
 def set_gemm_pairs(mode: int) -> None:
     """Process-wide default GEMM tile mode for the unit operators and for workspaces created
     afterwards (Workspace.set_gemm_pairs sets one workspace's): 0 = one SM per 128-row tile,
-    1 = SM pairs (256 x 192 where N allows, else 256 x 256), 2 = SM pairs, 256 x 256 first."""
+    1 = SM pairs (256 x 192 where N allows, else 256 x 256), 2 (default) = SM pairs, 256 x 256
+    first."""
     _check(lib().bbh_set_gemm_pairs(int(mode)))
 
 

@@ -289,7 +289,7 @@ struct bbh_ws {
   int32_t* meta = nullptr;
   int* err = nullptr;
   std::vector<GemmPlan> plans;  // 4 per layer: QKV, O+LN, FFN1+GELU, FFN2+LN
-  int gemm_pairs = 1;           // make_gemm_plan's pair_mode for this workspace's plans
+  int gemm_pairs = 2;           // make_gemm_plan's pair_mode for this workspace's plans
   bool plans_stale = false;     // the plans must be rebuilt (tile mode changed)
   bool l2_persist = false;      // forward launches carry an L2 access-policy window over the layer weights
   cudaAccessPolicyWindow l2_window{};

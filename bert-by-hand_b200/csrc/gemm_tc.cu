@@ -466,7 +466,7 @@ int set_gemm_residual(GemmPlan* plan, const __half* R, int ldr) {
   return encode_2d(&plan->tmR, R, plan->rows_cap, plan->p.N, ldr, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-static std::atomic<int> g_default_pair_mode{1};
+static std::atomic<int> g_default_pair_mode{2};
 int default_gemm_pair_mode() { return g_default_pair_mode.load(std::memory_order_relaxed); }
 void set_default_gemm_pair_mode(int mode) { g_default_pair_mode.store(mode, std::memory_order_relaxed); }
 

@@ -86,9 +86,11 @@ BBH_API void bbh_ws_free(bbh_ws* ws);
  * allocation, weight staging) while it finishes, and the next one waits for its results
  * before touching them; 0: plain stream order. Results are identical either way. */
 BBH_API int bbh_ws_set_pdl(bbh_ws* ws, int enable);
-/* GEMM tile shape: 0 = one SM per 128-row tile; 1 (default) = pairs of SMs sharing one
- * 256-row tile (tcgen05 cta_group::2), 192 columns wide where N allows, else 256; 2 = pairs,
- * 256 columns first. Modes 0 and 1 give bit-identical results.
+/* GEMM tile shape: 0 = one SM per 128-row tile; 1 = pairs of SMs sharing one 256-row tile
+ * (tcgen05 cta_group::2), 192 columns wide where N allows, else 256; 2 (default) = pairs,
+ * 256 columns first (the first FFN layer, N = 1536; QKV, N = 1152, stays at 192). In modes
+ * 1 and 2 the residual-LayerNorm GEMMs give each SM pair a whole 256 x 384 tile. All modes
+ * give bit-identical results.
  * bbh_ws_set_gemm_pairs sets it for one workspace (its plans are rebuilt by the next
  * forward; not while a forward of that workspace is being enqueued on another thread).
  * bbh_set_gemm_pairs sets the process-wide default (an atomic value) that workspaces
